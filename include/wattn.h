@@ -1,0 +1,266 @@
+/*
+ * wattn.h -- C ABI of the B200 (sm_100a) attention path for whisper.rs.
+ *
+ * This library replaces whisper.rs's attention hot path:
+ *   crates/tensor/src/ops/attention.rs      flash_attention_2 (:68),
+ *                                           multi_head_attention (:29),
+ *                                           single_token_mha_d64 (:246)
+ *   crates/whisper/src/decoder.rs           multi_head_attention_with_cache
+ *                                           (:835), DecoderKvCache (:131-264)
+ * Each entry point names the reference interface it stands in for.
+ *
+ * Conventions
+ *   - Layout is the reference's: per utterance a row-major [t][n_heads*64]
+ *     matrix, head h at columns h*64 .. h*64+63 (attention.rs:117,124). Every
+ *     device entry point also takes explicit row strides (in elements), so a
+ *     fused [T][3*d_model] QKV buffer can be passed without splitting it
+ *     (crates/whisper/src/encoder.rs:279-286).
+ *   - Head dimension must be 64 (every Whisper model); other values return
+ *     WATTN_ERR_UNSUPPORTED. There is no CPU fallback.
+ *   - Device entry points are asynchronous on the caller's stream
+ *     (a cudaStream_t passed as void*; NULL = legacy default stream) and take
+ *     device pointers only. Host entry points (wattn_*_host and the four
+ *     reference-signature mirrors) take host pointers and return when the
+ *     output is in host memory.
+ *   - Every function returns a status: 0 = OK, negative = error. Nothing
+ *     aborts or prints. wattn_last_error() gives the calling thread's last
+ *     error message. All entry points are thread-safe and re-entrant.
+ *   - Kernel-side waits are bounded; a wait that runs out sets a per-device
+ *     status word, read (and cleared) by wattn_device_status().
+ */
+#ifndef WATTN_H
+#define WATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------ status codes */
+#define WATTN_OK 0
+#define WATTN_ERR_INVALID (-1)     /* bad argument (the reference asserts) */
+#define WATTN_ERR_UNSUPPORTED (-2) /* e.g. head dimension != 64 */
+#define WATTN_ERR_CUDA (-3)        /* a CUDA runtime call failed */
+#define WATTN_ERR_TIMEOUT (-4)     /* a bounded device wait ran out */
+#define WATTN_ERR_NOMEM (-5)       /* device or page-pool memory exhausted */
+#define WATTN_ERR_RANGE (-6)       /* slot / layer / position out of range */
+
+/* ------------------------------------------------------------ element types */
+#define WATTN_F32 0
+#define WATTN_F16 1
+#define WATTN_BF16 2
+
+/* ABI version (major*10000 + minor*100 + patch). */
+int wattn_version(void);
+
+/* Static description of a status code. Never NULL. */
+const char *wattn_status_string(int status);
+
+/* Copies the calling thread's last error message into buf (NUL-terminated,
+ * truncated to len). Returns the status code of that error (0 if none). */
+int wattn_last_error(char *buf, size_t len);
+
+/* Reads and clears the device status word of `device` (the current device
+ * if device < 0): WATTN_OK, or WATTN_ERR_TIMEOUT if a kernel's bounded wait
+ * ran out since the last call. Synchronises that device. */
+int wattn_device_status(int device, int *status);
+
+/* ======================================================================
+ * Encoder / general attention (device pointers)
+ *
+ * Replaces flash_attention_2 / multi_head_attention
+ * (crates/tensor/src/ops/attention.rs:29-41, :68-242) for `batch`
+ * independent calls. O[b] = softmax(scale * Q[b] K[b]^T [+mask]) V[b] per
+ * head. causal != 0 masks key j for query i when j > i + q_pos_offset
+ * (q_pos_offset = 0 is attention.rs's causal rule :161-165; t_past is
+ * decoder.rs:864's). Rows whose every key is masked, and t_kv == 0, give 0.
+ *
+ * in_dtype  WATTN_F16 / WATTN_BF16: tcgen05 tensor-core kernel, f32
+ *           accumulation. WATTN_F32: f32 CUDA-core kernel (the reference's
+ *           own precision).
+ * out_dtype WATTN_F32, or the input type.
+ * Strides are in elements: *_row_stride between rows t and t+1 of one
+ * utterance, *_batch_stride between utterances. K and V share strides.
+ * 16-bit inputs need 16-byte aligned q/k/v and row/batch strides that are
+ * multiples of 8 elements; outputs need 16-byte aligned rows.
+ * ====================================================================== */
+int wattn_attention_fwd(const void *q, const void *k, const void *v, void *o,
+                        int in_dtype, int out_dtype, int batch, int t_q,
+                        int t_kv, int n_heads, int d_head,
+                        int64_t q_row_stride, int64_t kv_row_stride,
+                        int64_t o_row_stride, int64_t q_batch_stride,
+                        int64_t kv_batch_stride, int64_t o_batch_stride,
+                        float scale, int causal, int q_pos_offset,
+                        void *stream);
+
+/* ======================================================================
+ * Decoder decode attention over dense K/V (device pointers)
+ *
+ * Replaces single_token_mha_d64 (attention.rs:246-434), reached from
+ * flash_attention_2 for t_q == 1 (:102-104) and from the decoder's
+ * cross-attention (decoder.rs:698). n_groups groups of group_size query
+ * rows; every row of group g attends the same K/V block of t_kv rows
+ * (the beams of one utterance share its cross-attention K/V,
+ * decoder.rs:137-139). Query row r = g*group_size + i lives at
+ * q + r*q_row_stride, its output at o + r*o_row_stride; group g's keys at
+ * k + g*kv_group_stride + j*kv_row_stride (same for v).
+ *
+ * Split-KV: the keys are cut into chunks processed by separate CTAs and
+ * merged by a log-sum-exp reduction. `workspace` (device memory of at least
+ * wattn_decode_workspace_bytes() bytes, zero-filled before its first use and
+ * left zeroed by every call) holds the partials; pass NULL to use a
+ * library-owned per-device workspace.
+ * q_dtype / out_dtype: F32, F16 or BF16. kv_dtype: F32, F16 or BF16.
+ * ====================================================================== */
+size_t wattn_decode_workspace_bytes(int n_groups, int group_size, int t_kv,
+                                    int n_heads);
+
+int wattn_decode_fwd(const void *q, const void *k, const void *v, void *o,
+                     int q_dtype, int kv_dtype, int out_dtype, int n_groups,
+                     int group_size, int t_kv, int n_heads, int d_head,
+                     int64_t q_row_stride, int64_t kv_row_stride,
+                     int64_t kv_group_stride, int64_t o_row_stride,
+                     float scale, void *workspace, size_t workspace_bytes,
+                     void *stream);
+
+/* ======================================================================
+ * Device-resident paged KV cache (replaces DecoderKvCache,
+ * crates/whisper/src/decoder.rs:131-264, and the per-slot truncate/append
+ * of decode_batch_inner, decoder.rs:616-647)
+ *
+ * One cache holds the self-attention K/V of n_layers layers for a set of
+ * slots (beam hypotheses). Storage is a pool of pages on the device; a page
+ * holds page_rows consecutive positions of one slot for every layer, K and
+ * V, every head: [page][layer][K|V][head][page_rows][64]. A slot's history is
+ * its page table (host-side, mirrored to the device when it changes) plus
+ * a start offset (rows dropped by slide_to_fit) and its length t_past.
+ * Forking a slot (copy_slot) shares its full pages and copies only the
+ * partially filled last page; a shared page is copied before it is
+ * written (copy on write).
+ *
+ * Semantics follow the reference exactly: append() writes n rows at
+ * positions t_past .. t_past+n-1 after dropping rows >= t_past (the rewind
+ * of decoder.rs:631-633); attend() runs causal attention of those n rows
+ * over positions 0 .. t_past+i (decoder.rs:835-892); advance() adds n to
+ * t_past after the last layer (decoder.rs:765-767).
+ * All functions taking a stream enqueue their device work on it; the others
+ * only change host-side state.
+ * ====================================================================== */
+typedef struct wattn_kv_cache wattn_kv_cache;
+
+/* DecoderKvCache::new (decoder.rs:147). n_pages = 0 sizes the pool for every
+ * slot at max_ctx plus one copy-on-write page per slot. The cache lives on
+ * the current device. */
+int wattn_kv_create(wattn_kv_cache **out, int n_layers, int n_slots,
+                    int n_heads, int d_head, int max_ctx, int page_rows,
+                    int n_pages, int dtype);
+int wattn_kv_destroy(wattn_kv_cache *cache);
+
+int wattn_kv_clear(wattn_kv_cache *cache);                 /* :161-173 */
+int wattn_kv_clear_slot(wattn_kv_cache *cache, int slot);  /* :176-186 */
+int wattn_kv_ensure_slots(wattn_kv_cache *cache, int n_slots); /* :203-214 */
+int wattn_kv_copy_slot(wattn_kv_cache *cache, int dst, int src,
+                       void *stream);                      /* :220-234 */
+int wattn_kv_slot_len(const wattn_kv_cache *cache, int slot,
+                      int *len);                           /* :237-239 */
+int wattn_kv_slide_to_fit(wattn_kv_cache *cache, int slot, int n_new,
+                          int max_ctx, int *pos);          /* :248-263 */
+/* The C API rewind: whisper_decode_with_state sets t_past = n_past
+ * (crates/ffi/src/lib.rs:2352). Rows >= n_past are dropped by the next
+ * append. n_past may not exceed the slot's current length. */
+int wattn_kv_set_t_past(wattn_kv_cache *cache, int slot, int n_past);
+/* t_past[slots[i]] += n_tokens[i] (decoder.rs:765-767). */
+int wattn_kv_advance(wattn_kv_cache *cache, const int *slots,
+                     const int *n_tokens, int n_seqs);
+
+/* Append n_tokens[i] new K/V rows for slots[i] into `layer`
+ * (decoder.rs:631-635). Rows are packed sequence-major as in the reference
+ * (k_rows + (sum_{i'<i} n_tokens[i'] + t) * row_stride), width
+ * n_heads*64, type src_dtype. slots / n_tokens are host arrays. */
+int wattn_kv_append(wattn_kv_cache *cache, int layer, const int *slots,
+                    const int *n_tokens, int n_seqs, const void *k_rows,
+                    const void *v_rows, int src_dtype, int64_t row_stride,
+                    void *stream);
+
+/* Causal self-attention of the appended rows over each slot's history in
+ * `layer` (multi_head_attention_with_cache, decoder.rs:835-892). q / o rows
+ * packed like k_rows above. `workspace` as for wattn_decode_fwd
+ * (wattn_kv_workspace_bytes), or NULL. */
+size_t wattn_kv_workspace_bytes(const wattn_kv_cache *cache, int n_rows);
+int wattn_kv_attend(wattn_kv_cache *cache, int layer, const int *slots,
+                    const int *n_tokens, int n_seqs, const void *q,
+                    int q_dtype, int64_t q_row_stride, void *o, int out_dtype,
+                    int64_t o_row_stride, float scale, void *workspace,
+                    size_t workspace_bytes, void *stream);
+
+/* Device copy of one slot's rows of one layer, in the reference's flat
+ * layout ([t_past][n_heads*64], dtype out_dtype), for inspection and tests
+ * (the k_self / v_self fields of decoder.rs:133-135). `which` 0 = K, 1 = V. */
+int wattn_kv_read_slot(wattn_kv_cache *cache, int layer, int slot, int which,
+                       void *out, int out_dtype, void *stream);
+
+/* Pool statistics: pages in use and pool size. */
+int wattn_kv_stats(const wattn_kv_cache *cache, int *pages_used,
+                   int *pages_total);
+
+/* ======================================================================
+ * Host-buffer entry points (the reference-facing calls)
+ *
+ * Same math as the device entry points, on host buffers: inputs are copied
+ * to the current device, computed, and copied back before returning. Each
+ * calling thread gets its own device buffers and streams, kept between
+ * calls. Pinned (page-locked) host buffers give full copy bandwidth; large
+ * batches are processed in chunks whose copies overlap the kernels.
+ * ====================================================================== */
+
+/* flash_attention_2 (attention.rs:68), f32 host slices, one utterance:
+ * q [t_q][d_model], k/v [t_kv][d_model], output [t_q][d_model]. */
+int wattn_flash_attention_2(const float *q, const float *k, const float *v,
+                            size_t t_q, size_t t_kv, size_t n_heads,
+                            size_t d_model, int causal, float *output);
+
+/* multi_head_attention (attention.rs:29): same as flash_attention_2. */
+int wattn_multi_head_attention(const float *q, const float *k, const float *v,
+                               size_t t_q, size_t t_kv, size_t n_heads,
+                               size_t d_model, int causal, float *output);
+
+/* single_token_mha_d64 (attention.rs:246): one query row, t_kv keys. */
+int wattn_single_token_mha_d64(const float *q, const float *k, const float *v,
+                               size_t t_kv, size_t n_heads, size_t d_model,
+                               float *output);
+
+/* multi_head_attention_with_cache (decoder.rs:835): n_tokens queries at
+ * positions t_past .. t_past+n_tokens-1 over total_tokens cached rows. */
+int wattn_multi_head_attention_with_cache(const float *q, const float *k,
+                                          const float *v, size_t n_tokens,
+                                          size_t total_tokens, size_t t_past,
+                                          size_t n_heads, size_t d_model,
+                                          float *output);
+
+/* Batched host-buffer encoder attention: contiguous [batch][t][n_heads*64]
+ * host buffers of in_dtype; output [batch][t_q][n_heads*64] of out_dtype. */
+int wattn_attention_host(const void *q, const void *k, const void *v, void *o,
+                         int in_dtype, int out_dtype, int batch, int t_q,
+                         int t_kv, int n_heads, float scale, int causal);
+
+/* Batched host-buffer decode: q [n_groups*group_size][n_heads*64] (q_dtype),
+ * k/v [n_groups][t_kv][n_heads*64] (kv_dtype), o like q (out_dtype). */
+int wattn_decode_host(const void *q, const void *k, const void *v, void *o,
+                      int q_dtype, int kv_dtype, int out_dtype, int n_groups,
+                      int group_size, int t_kv, int n_heads, float scale);
+
+/* ======================================================================
+ * Self-test of the bounded-wait machinery: launches one kernel that waits,
+ * with a limit of `limit_us` microseconds, on a device flag that nothing
+ * sets, then reports through the device status word. Returns
+ * WATTN_ERR_TIMEOUT when the wait ran out as designed (and the device stays
+ * usable), WATTN_OK if the flag was somehow set.
+ * ====================================================================== */
+int wattn_selftest_bounded_wait(int limit_us, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* WATTN_H */

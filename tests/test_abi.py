@@ -1,0 +1,91 @@
+"""The C-ABI library loads, exports every symbol include/wattn.h declares,
+and rejects bad arguments before touching a GPU (no compute calls here)."""
+import ctypes
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "wattn.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(wattn_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def wattn():
+    import wattn as W
+    return W
+
+
+def test_header_declares_the_entry_points():
+    syms = declared_symbols()
+    for must in ("wattn_attention_fwd", "wattn_decode_fwd", "wattn_kv_create", "wattn_kv_attend",
+                 "wattn_flash_attention_2", "wattn_single_token_mha_d64",
+                 "wattn_multi_head_attention_with_cache", "wattn_last_error"):
+        assert must in syms
+
+
+def test_library_exports_every_declared_symbol(wattn):
+    out = subprocess.run(["nm", "-D", "--defined-only", wattn.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = set(re.findall(r"\bT (wattn_[a-z0-9_]+)$", out, flags=re.M))
+    missing = [s for s in declared_symbols() if s not in exported]
+    assert not missing, missing
+    # and the Python host module binds exactly the declared set
+    assert sorted(wattn.EXPORTED_SYMBOLS) == declared_symbols()
+
+
+def test_status_strings(wattn):
+    assert wattn.status_string(0) == "ok"
+    assert "unsupported" in wattn.status_string(-2)
+    assert wattn.lib.wattn_version() >= 100
+
+
+def test_reference_asserts_become_errors(wattn):
+    # attention.rs:79-84: n_heads == 0 and d_model % n_heads != 0 are asserts;
+    # here they are WATTN_ERR_INVALID, and d_head != 64 is WATTN_ERR_UNSUPPORTED.
+    # All are rejected before any CUDA call.
+    q = np.zeros(128 * 4, np.float32)
+    o = np.zeros_like(q)
+    with pytest.raises(wattn.WattnError) as e:
+        wattn.flash_attention_2(q, q, q, 4, 4, 0, 128, False, o)
+    assert e.value.status == -1
+    with pytest.raises(wattn.WattnError) as e:
+        wattn.flash_attention_2(q, q, q, 4, 4, 3, 128, False, o)
+    assert e.value.status == -1
+    qq = np.zeros(160 * 4, np.float32)
+    with pytest.raises(wattn.WattnError) as e:
+        wattn.flash_attention_2(qq, qq, qq, 4, 4, 2, 160, False, np.zeros_like(qq))
+    assert e.value.status == -2
+    with pytest.raises(wattn.WattnError) as e:  # length mismatch (attention.rs:85-88)
+        wattn.flash_attention_2(q, q, q, 5, 4, 2, 128, False, o)
+    assert e.value.status == -1
+    # no-op shapes return before touching a device
+    wattn.flash_attention_2(np.zeros(0, np.float32), q, q, 0, 4, 2, 128, False,
+                            np.zeros(0, np.float32))
+
+
+def test_device_entry_points_validate_first(wattn):
+    L = wattn.lib
+    # head dim 80 -> unsupported, before any pointer is touched
+    rc = L.wattn_attention_fwd(None, None, None, None, 1, 1, 1, 4, 4, 2, 80, 160, 160, 160, 0, 0, 0,
+                               0.125, 0, 0, None)
+    assert rc == -2
+    buf = ctypes.create_string_buffer(256)
+    assert L.wattn_last_error(buf, 256) == -2 and b"head dimension" in buf.value
+    # negative scale, bad dtype
+    assert L.wattn_attention_fwd(None, None, None, None, 1, 1, 1, 4, 4, 2, 64, 128, 128, 128, 0, 0,
+                                 0, -1.0, 0, 0, None) == -1
+    assert L.wattn_decode_fwd(None, None, None, None, 7, 1, 1, 1, 1, 10, 2, 64, 128, 128, 0, 128,
+                              0.125, None, 0, None) == -1
+    # zero-size calls are valid no-ops
+    assert L.wattn_attention_fwd(None, None, None, None, 1, 1, 0, 4, 4, 2, 64, 128, 128, 128, 0, 0,
+                                 0, 0.125, 0, 0, None) == 0
+    assert L.wattn_decode_workspace_bytes(32, 5, 1500, 20) > 0

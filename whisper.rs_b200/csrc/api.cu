@@ -1,0 +1,670 @@
+// api.cu -- the extern "C" boundary: argument checks, dispatch to the
+// kernels, error reporting, host-buffer entry points and the bounded-wait
+// self-test. Declarations and contracts are in include/wattn.h.
+
+#include <cudaTypedefs.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <mutex>
+#include <vector>
+
+#include "wattn_common.cuh"
+#include "wattn_internal.h"
+
+namespace wattn {
+
+__device__ int g_status = WATTN_OK;
+
+namespace {
+
+thread_local int t_err_status = WATTN_OK;
+thread_local char t_err_msg[512] = {0};
+
+constexpr int kMaxDevices = 64;
+std::mutex g_mu;
+int *g_status_ptr[kMaxDevices] = {nullptr};
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+}  // namespace
+
+int set_error(int status, const char *fmt, ...) {
+  t_err_status = status;
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_err_msg, sizeof(t_err_msg), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+void clear_error() {
+  t_err_status = WATTN_OK;
+  t_err_msg[0] = 0;
+}
+
+int check_launch(const char *what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) return WATTN_OK;
+  return set_error(WATTN_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+int *device_status_ptr() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    set_error(WATTN_ERR_CUDA, "no current CUDA device");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_status_ptr[dev] == nullptr) {
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_status) != cudaSuccess) {
+      check_launch("cudaGetSymbolAddress(status word)");
+      return nullptr;
+    }
+    g_status_ptr[dev] = static_cast<int *>(p);
+  }
+  return g_status_ptr[dev];
+}
+
+int encode_tmap(CUtensorMap *map, CUtensorMapDataType dtype, uint32_t rank, const void *base,
+                const uint64_t *dims, const uint64_t *strides_bytes, const uint32_t *box,
+                CUtensorMapSwizzle swizzle) {
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_encode == nullptr) {
+      void *fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
+              cudaSuccess ||
+          q != cudaDriverEntryPointSuccess || fn == nullptr) {
+        cudaGetLastError();
+        return set_error(WATTN_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+      }
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+  }
+  cuuint64_t d[5];
+  cuuint64_t s[4];
+  cuuint32_t b[5], e[5];
+  for (uint32_t i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+    if (i + 1 < rank) s[i] = strides_bytes[i];
+  }
+  const CUresult r = g_encode(map, dtype, rank, const_cast<void *>(base), d, s, b, e,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(WATTN_ERR_INVALID,
+                     "TMA descriptor rejected (error %d): base %p must be 16-byte aligned and "
+                     "row strides multiples of 16 bytes",
+                     (int)r, base);
+  return WATTN_OK;
+}
+
+namespace {
+
+struct Workspace {
+  void *ptr = nullptr;
+  size_t bytes = 0;
+};
+thread_local Workspace t_ws[kMaxDevices];
+
+}  // namespace
+
+void *thread_workspace(size_t bytes, cudaStream_t stream) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kMaxDevices) return nullptr;
+  Workspace &w = t_ws[dev];
+  if (w.bytes < bytes) {
+    if (w.ptr) {
+      cudaDeviceSynchronize();
+      cudaFree(w.ptr);
+    }
+    w.ptr = nullptr;
+    w.bytes = 0;
+    const size_t sz = std::max(bytes, (size_t)1 << 20);
+    if (cudaMalloc(&w.ptr, sz) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    if (cudaMemsetAsync(w.ptr, 0, sz, stream) != cudaSuccess) {
+      cudaGetLastError();
+      cudaFree(w.ptr);
+      w.ptr = nullptr;
+      return nullptr;
+    }
+    w.bytes = sz;
+  }
+  return w.ptr;
+}
+
+namespace {
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+__global__ void bounded_wait_kernel(volatile int *flag, int *status,
+                                    unsigned long long limit_ns) {
+  const unsigned long long t0 = globaltimer_ns();
+  while (*flag == 0) {
+    if (globaltimer_ns() - t0 > limit_ns) {
+      report_timeout(status);
+      return;
+    }
+    __nanosleep(1000);
+  }
+}
+
+// ----------------------------------------------------------- host contexts
+// Per calling thread and device: two streams and their device buffers, so a
+// host-buffer call can overlap the copies of one chunk with the kernel of
+// the previous one.
+struct HostCtx {
+  cudaStream_t st[2] = {nullptr, nullptr};
+  void *buf[2] = {nullptr, nullptr};
+  size_t buf_bytes[2] = {0, 0};
+  void *ws[2] = {nullptr, nullptr};
+  size_t ws_bytes[2] = {0, 0};
+  bool ok = false;
+};
+thread_local HostCtx t_host[kMaxDevices];
+
+HostCtx *host_ctx() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    set_error(WATTN_ERR_CUDA, "no current CUDA device");
+    return nullptr;
+  }
+  HostCtx &h = t_host[dev];
+  if (!h.ok) {
+    for (int i = 0; i < 2; ++i)
+      if (cudaStreamCreateWithFlags(&h.st[i], cudaStreamNonBlocking) != cudaSuccess) {
+        check_launch("cudaStreamCreate");
+        return nullptr;
+      }
+    h.ok = true;
+  }
+  return &h;
+}
+
+int grow(void **p, size_t *have, size_t need, bool zero, cudaStream_t st) {
+  if (*have >= need) return WATTN_OK;
+  if (*p) {
+    cudaStreamSynchronize(st);
+    cudaFree(*p);
+  }
+  *p = nullptr;
+  *have = 0;
+  if (cudaMalloc(p, need) != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(WATTN_ERR_NOMEM, "cudaMalloc(%zu) failed", need);
+  }
+  if (zero && cudaMemsetAsync(*p, 0, need, st) != cudaSuccess) return check_launch("cudaMemsetAsync");
+  *have = need;
+  return WATTN_OK;
+}
+
+int h2d(void *dst, const void *src, size_t n, cudaStream_t st) {
+  if (n == 0) return WATTN_OK;
+  if (cudaMemcpyAsync(dst, src, n, cudaMemcpyHostToDevice, st) != cudaSuccess)
+    return check_launch("cudaMemcpyAsync H2D");
+  return WATTN_OK;
+}
+int d2h(void *dst, const void *src, size_t n, cudaStream_t st) {
+  if (n == 0) return WATTN_OK;
+  if (cudaMemcpyAsync(dst, src, n, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return check_launch("cudaMemcpyAsync D2H");
+  return WATTN_OK;
+}
+
+// Ends a host-buffer call: waits for both streams, then reports CUDA errors
+// and the device status word.
+int finish_host(HostCtx *h, int rc) {
+  for (int i = 0; i < 2; ++i)
+    if (cudaStreamSynchronize(h->st[i]) != cudaSuccess && rc == WATTN_OK)
+      rc = check_launch("cudaStreamSynchronize");
+  if (rc != WATTN_OK) return rc;
+  int *sp = device_status_ptr();
+  int s = WATTN_OK;
+  if (sp && cudaMemcpy(&s, sp, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess &&
+      s != WATTN_OK) {
+    const int zero = WATTN_OK;
+    cudaMemcpy(sp, &zero, sizeof(int), cudaMemcpyHostToDevice);
+    return set_error(s, "a kernel's bounded wait ran out");
+  }
+  return WATTN_OK;
+}
+
+// Bytes that one utterance moves through a host-buffer attention call.
+struct AttnSizes {
+  size_t q, kv, o;
+};
+
+// Shape, type and scalar checks shared by the device and host entry points.
+int validate_attention_shape(int in_dt, int out_dt, int batch, int t_q, int t_kv, int n_heads,
+                             int d_head, float scale, int causal, int q_pos_offset) {
+  if (d_head != kHeadDim)
+    return set_error(WATTN_ERR_UNSUPPORTED, "head dimension %d is not supported (64 only)", d_head);
+  if (!valid_dtype(in_dt) || !valid_dtype(out_dt))
+    return set_error(WATTN_ERR_INVALID, "unknown dtype (%d, %d)", in_dt, out_dt);
+  if (out_dt != WATTN_F32 && out_dt != in_dt)
+    return set_error(WATTN_ERR_INVALID, "out_dtype must be F32 or the input type");
+  if (batch < 0 || t_q < 0 || t_kv < 0 || n_heads <= 0)
+    return set_error(WATTN_ERR_INVALID, "negative size or n_heads <= 0");
+  if (batch > 65535 || n_heads > 65535)
+    return set_error(WATTN_ERR_INVALID, "batch and n_heads must be <= 65535");
+  if (!(scale > 0.f) || scale > 3.0e38f)
+    return set_error(WATTN_ERR_INVALID, "scale must be finite and positive");
+  if (causal && q_pos_offset < 0) return set_error(WATTN_ERR_INVALID, "q_pos_offset must be >= 0");
+  return WATTN_OK;
+}
+
+int validate_attention(const void *q, const void *k, const void *v, const void *o, int in_dt,
+                       int out_dt, int batch, int t_q, int t_kv, int n_heads, int d_head,
+                       int64_t q_rs, int64_t kv_rs, int64_t o_rs, int64_t q_bs, int64_t kv_bs,
+                       int64_t o_bs, float scale, int causal, int q_pos_offset) {
+  int rc = validate_attention_shape(in_dt, out_dt, batch, t_q, t_kv, n_heads, d_head, scale,
+                                    causal, q_pos_offset);
+  if (rc != WATTN_OK) return rc;
+  const int64_t w = (int64_t)n_heads * kHeadDim;
+  if (q_rs < w || kv_rs < w || o_rs < w)
+    return set_error(WATTN_ERR_INVALID, "row strides must be >= n_heads * 64");
+  if (q_bs < 0 || kv_bs < 0 || o_bs < 0) return set_error(WATTN_ERR_INVALID, "negative batch stride");
+  if (batch == 0 || t_q == 0) return WATTN_OK;
+  if (!q || !o || (t_kv > 0 && (!k || !v))) return set_error(WATTN_ERR_INVALID, "NULL tensor");
+  const int es_in = elem_size(in_dt), es_out = elem_size(out_dt);
+  const int64_t unit = 16 / es_in;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || q_rs % unit || kv_rs % unit ||
+      q_bs % unit || kv_bs % unit)
+    return set_error(WATTN_ERR_INVALID,
+                     "q/k/v must be 16-byte aligned with row and batch strides that are "
+                     "multiples of 16 bytes");
+  if (!aligned16(o) || (o_rs * es_out) % 16 || (o_bs * es_out) % 16)
+    return set_error(WATTN_ERR_INVALID, "o must be 16-byte aligned with 16-byte multiple strides");
+  return WATTN_OK;
+}
+
+int attention_device(const void *q, const void *k, const void *v, void *o, int in_dt, int out_dt,
+                     int batch, int t_q, int t_kv, int n_heads, int64_t q_rs, int64_t kv_rs,
+                     int64_t o_rs, int64_t q_bs, int64_t kv_bs, int64_t o_bs, float scale,
+                     int causal, int q_pos_offset, cudaStream_t st) {
+  if (batch == 0 || t_q == 0) return WATTN_OK;
+  if (t_kv == 0) return launch_zero_rows(o, out_dt, batch, t_q, n_heads * kHeadDim, o_rs, o_bs, st);
+  if (in_dt == WATTN_F32)
+    return launch_attn_f32((const float *)q, (const float *)k, (const float *)v, (float *)o, batch,
+                           t_q, t_kv, n_heads, q_rs, kv_rs, o_rs, q_bs, kv_bs, o_bs, scale,
+                           causal, q_pos_offset, st);
+  return launch_attn_tc(q, k, v, o, in_dt, out_dt, batch, t_q, t_kv, n_heads, q_rs, kv_rs, o_rs,
+                        q_bs, kv_bs, o_bs, scale, causal, q_pos_offset, st);
+}
+
+int validate_decode(const void *q, const void *k, const void *v, const void *o, int q_dt,
+                    int kv_dt, int out_dt, int n_groups, int group_size, int t_kv, int n_heads,
+                    int d_head, int64_t q_rs, int64_t kv_rs, int64_t kv_gs, int64_t o_rs,
+                    float scale) {
+  if (d_head != kHeadDim)
+    return set_error(WATTN_ERR_UNSUPPORTED, "head dimension %d is not supported (64 only)", d_head);
+  if (!valid_dtype(q_dt) || !valid_dtype(kv_dt) || !valid_dtype(out_dt))
+    return set_error(WATTN_ERR_INVALID, "unknown dtype");
+  if (n_groups < 0 || group_size <= 0 || t_kv < 0 || n_heads <= 0)
+    return set_error(WATTN_ERR_INVALID, "invalid sizes");
+  if (n_heads > 65535) return set_error(WATTN_ERR_INVALID, "n_heads must be <= 65535");
+  if ((int64_t)n_groups * ((group_size + 7) / 8) > 65535)
+    return set_error(WATTN_ERR_INVALID, "too many query row groups in one call (max 65535 x 8 rows)");
+  if (!(scale > 0.f) || scale > 3.0e38f)
+    return set_error(WATTN_ERR_INVALID, "scale must be finite and positive");
+  const int64_t w = (int64_t)n_heads * kHeadDim;
+  if (q_rs < w || kv_rs < w || o_rs < w) return set_error(WATTN_ERR_INVALID, "row strides must be >= n_heads * 64");
+  if (kv_gs < 0) return set_error(WATTN_ERR_INVALID, "negative group stride");
+  if (n_groups == 0) return WATTN_OK;
+  if (!q || !o || (t_kv > 0 && (!k || !v))) return set_error(WATTN_ERR_INVALID, "NULL tensor");
+  const int es = elem_size(kv_dt);
+  if (!aligned16(k) || !aligned16(v) || (kv_rs * es) % 16 || (kv_gs * es) % 16)
+    return set_error(WATTN_ERR_INVALID,
+                     "k/v must be 16-byte aligned with row and group strides that are multiples "
+                     "of 16 bytes");
+  return WATTN_OK;
+}
+
+int decode_device(const void *q, const void *k, const void *v, void *o, int q_dt, int kv_dt,
+                  int out_dt, int n_groups, int group_size, int t_kv, int n_heads, int64_t q_rs,
+                  int64_t kv_rs, int64_t kv_gs, int64_t o_rs, float scale, void *ws,
+                  size_t ws_bytes, cudaStream_t st) {
+  if (n_groups == 0) return WATTN_OK;
+  if (t_kv == 0)
+    return launch_zero_rows(o, out_dt, 1, n_groups * group_size, n_heads * kHeadDim, o_rs, 0, st);
+  if (ws == nullptr) {
+    const DecodePlan pl = plan_decode(n_groups, group_size, t_kv, n_heads, kv_dt);
+    ws = thread_workspace(pl.workspace_bytes, st);
+    if (ws == nullptr) return set_error(WATTN_ERR_NOMEM, "decode workspace allocation failed");
+    ws_bytes = std::max(pl.workspace_bytes, (size_t)1 << 20);
+  }
+  return launch_decode(q, k, v, o, q_dt, kv_dt, out_dt, n_groups, group_size, t_kv, n_heads, q_rs,
+                       kv_rs, kv_gs, o_rs, scale, ws, ws_bytes, st);
+}
+
+size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Host-buffer attention over contiguous [batch][t][w] buffers, in chunks of
+// utterances alternating between two streams.
+int attention_host(const void *q, const void *k, const void *v, void *o, int in_dt, int out_dt,
+                   int batch, int t_q, int t_kv, int n_heads, float scale, int causal,
+                   int q_pos_offset) {
+  const int w = n_heads * kHeadDim;
+  // Host pointers need no alignment: the device copies made below are aligned.
+  int rc = validate_attention_shape(in_dt, out_dt, batch, t_q, t_kv, n_heads, kHeadDim, scale,
+                                    causal, q_pos_offset);
+  if (rc != WATTN_OK) return rc;
+  if (batch == 0 || t_q == 0) return WATTN_OK;
+  if (!q || !o || (t_kv > 0 && (!k || !v))) return set_error(WATTN_ERR_INVALID, "NULL buffer");
+  HostCtx *h = host_ctx();
+  if (!h) return WATTN_ERR_CUDA;
+  const size_t es_in = elem_size(in_dt), es_out = elem_size(out_dt);
+  const size_t qb = (size_t)t_q * w * es_in, kvb = (size_t)t_kv * w * es_in,
+               ob = (size_t)t_q * w * es_out;
+  const size_t per = round_up(qb, 256) + 2 * round_up(kvb, 256) + round_up(ob, 256);
+  // ~64 MB of device staging per stream, at least one utterance.
+  const int chunk = (int)std::max<size_t>(1, std::min<size_t>(batch, ((size_t)64 << 20) / per));
+  for (int i = 0; i < 2; ++i)
+    if ((rc = grow(&h->buf[i], &h->buf_bytes[i], per * chunk, false, h->st[i])) != WATTN_OK)
+      return finish_host(h, rc);
+  for (int c0 = 0, ci = 0; c0 < batch; c0 += chunk, ++ci) {
+    const int nb = std::min(chunk, batch - c0);
+    cudaStream_t st = h->st[ci & 1];
+    uint8_t *base = (uint8_t *)h->buf[ci & 1];
+    uint8_t *dq = base, *dk = dq + round_up(qb, 256) * nb, *dv = dk + round_up(kvb, 256) * nb,
+            *dout = dv + round_up(kvb, 256) * nb;
+    // Packed per chunk: [nb][t][w] with utterance stride = its byte size rounded to 256.
+    const int64_t qbs = round_up(qb, 256) / es_in, kvbs = round_up(kvb, 256) / es_in,
+                  obs = round_up(ob, 256) / es_out;
+    for (int b = 0; b < nb && rc == WATTN_OK; ++b) {
+      rc = h2d(dq + round_up(qb, 256) * b, (const uint8_t *)q + (c0 + b) * qb, qb, st);
+      if (rc == WATTN_OK) rc = h2d(dk + round_up(kvb, 256) * b, (const uint8_t *)k + (c0 + b) * kvb, kvb, st);
+      if (rc == WATTN_OK) rc = h2d(dv + round_up(kvb, 256) * b, (const uint8_t *)v + (c0 + b) * kvb, kvb, st);
+    }
+    if (rc == WATTN_OK)
+      rc = attention_device(dq, dk, dv, dout, in_dt, out_dt, nb, t_q, t_kv, n_heads, w, w, w, qbs,
+                            kvbs, obs, scale, causal, q_pos_offset, st);
+    for (int b = 0; b < nb && rc == WATTN_OK; ++b)
+      rc = d2h((uint8_t *)o + (c0 + b) * ob, dout + round_up(ob, 256) * b, ob, st);
+    if (rc != WATTN_OK) break;
+  }
+  return finish_host(h, rc);
+}
+
+// Host-buffer decode: q [n_groups*G][w], k/v [n_groups][t_kv][w], o like q.
+int decode_host(const void *q, const void *k, const void *v, void *o, int q_dt, int kv_dt,
+                int out_dt, int n_groups, int group_size, int t_kv, int n_heads, int64_t kv_rs,
+                float scale) {
+  const int w = n_heads * kHeadDim;
+  if (!valid_dtype(q_dt) || !valid_dtype(kv_dt) || !valid_dtype(out_dt) || n_groups < 0 ||
+      group_size <= 0 || t_kv < 0 || n_heads <= 0 || kv_rs < w || !(scale > 0.f))
+    return set_error(WATTN_ERR_INVALID, "decode_host: invalid arguments");
+  if (n_groups == 0) return WATTN_OK;
+  if (!q || !o || (t_kv > 0 && (!k || !v))) return set_error(WATTN_ERR_INVALID, "decode_host: NULL tensor");
+  HostCtx *h = host_ctx();
+  if (!h) return WATTN_ERR_CUDA;
+  const size_t es_q = elem_size(q_dt), es_kv = elem_size(kv_dt), es_o = elem_size(out_dt);
+  const int64_t dkv_rs = round_up((size_t)w, 16 / es_kv);  // device row stride (16-byte multiple)
+  const size_t qb = (size_t)group_size * w * es_q, ob = (size_t)group_size * w * es_o;
+  const size_t kvb_host = (size_t)t_kv * kv_rs * es_kv;
+  const size_t kvb_dev = round_up((size_t)t_kv * dkv_rs * es_kv, 256);
+  const size_t per = round_up(qb, 256) + 2 * kvb_dev + round_up(ob, 256);
+  const int chunk = (int)std::max<size_t>(1, std::min<size_t>(n_groups, ((size_t)64 << 20) / per));
+  int rc = WATTN_OK;
+  const DecodePlan pl = plan_decode(chunk, group_size, t_kv, n_heads, kv_dt);
+  for (int i = 0; i < 2 && rc == WATTN_OK; ++i) {
+    rc = grow(&h->buf[i], &h->buf_bytes[i], per * chunk, false, h->st[i]);
+    if (rc == WATTN_OK) rc = grow(&h->ws[i], &h->ws_bytes[i], pl.workspace_bytes, true, h->st[i]);
+  }
+  if (rc != WATTN_OK) return finish_host(h, rc);
+  for (int c0 = 0, ci = 0; c0 < n_groups; c0 += chunk, ++ci) {
+    const int ng = std::min(chunk, n_groups - c0);
+    cudaStream_t st = h->st[ci & 1];
+    uint8_t *base = (uint8_t *)h->buf[ci & 1];
+    uint8_t *dq = base, *dk = dq + round_up(qb, 256) * chunk, *dv = dk + kvb_dev * chunk,
+            *dout = dv + kvb_dev * chunk;
+    rc = h2d(dq, (const uint8_t *)q + (size_t)c0 * qb, qb * ng, st);  // rows contiguous
+    for (int g = 0; g < ng && rc == WATTN_OK; ++g) {
+      const uint8_t *ks = (const uint8_t *)k + (size_t)(c0 + g) * kvb_host;
+      const uint8_t *vs = (const uint8_t *)v + (size_t)(c0 + g) * kvb_host;
+      if (dkv_rs == kv_rs) {
+        rc = h2d(dk + kvb_dev * g, ks, kvb_host, st);
+        if (rc == WATTN_OK) rc = h2d(dv + kvb_dev * g, vs, kvb_host, st);
+      } else {
+        if (cudaMemcpy2DAsync(dk + kvb_dev * g, dkv_rs * es_kv, ks, kv_rs * es_kv, w * es_kv, t_kv,
+                              cudaMemcpyHostToDevice, st) != cudaSuccess ||
+            cudaMemcpy2DAsync(dv + kvb_dev * g, dkv_rs * es_kv, vs, kv_rs * es_kv, w * es_kv, t_kv,
+                              cudaMemcpyHostToDevice, st) != cudaSuccess)
+          rc = check_launch("cudaMemcpy2DAsync");
+      }
+    }
+    if (rc == WATTN_OK)
+      rc = decode_device(dq, dk, dv, dout, q_dt, kv_dt, out_dt, ng, group_size, t_kv, n_heads, w,
+                         dkv_rs, (int64_t)(kvb_dev / es_kv), w, scale, h->ws[ci & 1],
+                         h->ws_bytes[ci & 1], st);
+    if (rc == WATTN_OK) rc = d2h((uint8_t *)o + (size_t)c0 * ob, dout, ob * ng, st);
+    if (rc != WATTN_OK) break;
+  }
+  return finish_host(h, rc);
+}
+
+}  // namespace
+}  // namespace wattn
+
+using namespace wattn;
+
+extern "C" {
+
+int wattn_version(void) { return 100; }
+
+const char *wattn_status_string(int status) {
+  switch (status) {
+    case WATTN_OK: return "ok";
+    case WATTN_ERR_INVALID: return "invalid argument";
+    case WATTN_ERR_UNSUPPORTED: return "unsupported configuration";
+    case WATTN_ERR_CUDA: return "CUDA error";
+    case WATTN_ERR_TIMEOUT: return "bounded device wait ran out";
+    case WATTN_ERR_NOMEM: return "out of memory";
+    case WATTN_ERR_RANGE: return "out of range";
+    default: return "unknown status";
+  }
+}
+
+int wattn_last_error(char *buf, size_t len) {
+  if (buf && len > 0) {
+    strncpy(buf, t_err_msg, len - 1);
+    buf[len - 1] = 0;
+  }
+  return t_err_status;
+}
+
+int wattn_device_status(int device, int *status) {
+  clear_error();
+  if (!status) return set_error(WATTN_ERR_INVALID, "status is NULL");
+  int prev = 0;
+  cudaGetDevice(&prev);
+  if (device >= 0 && device != prev && cudaSetDevice(device) != cudaSuccess)
+    return check_launch("cudaSetDevice");
+  int rc = WATTN_OK;
+  int *sp = device_status_ptr();
+  if (!sp) rc = WATTN_ERR_CUDA;
+  if (rc == WATTN_OK && cudaDeviceSynchronize() != cudaSuccess) rc = check_launch("cudaDeviceSynchronize");
+  int s = WATTN_OK;
+  if (rc == WATTN_OK && cudaMemcpy(&s, sp, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+    rc = check_launch("read status word");
+  const int zero = WATTN_OK;
+  if (rc == WATTN_OK && cudaMemcpy(sp, &zero, sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess)
+    rc = check_launch("clear status word");
+  if (device >= 0 && device != prev) cudaSetDevice(prev);
+  *status = s;
+  return rc;
+}
+
+int wattn_attention_fwd(const void *q, const void *k, const void *v, void *o, int in_dtype,
+                        int out_dtype, int batch, int t_q, int t_kv, int n_heads, int d_head,
+                        int64_t q_row_stride, int64_t kv_row_stride, int64_t o_row_stride,
+                        int64_t q_batch_stride, int64_t kv_batch_stride, int64_t o_batch_stride,
+                        float scale, int causal, int q_pos_offset, void *stream) {
+  clear_error();
+  int rc = validate_attention(q, k, v, o, in_dtype, out_dtype, batch, t_q, t_kv, n_heads, d_head,
+                              q_row_stride, kv_row_stride, o_row_stride, q_batch_stride,
+                              kv_batch_stride, o_batch_stride, scale, causal, q_pos_offset);
+  if (rc != WATTN_OK) return rc;
+  return attention_device(q, k, v, o, in_dtype, out_dtype, batch, t_q, t_kv, n_heads, q_row_stride,
+                          kv_row_stride, o_row_stride, q_batch_stride, kv_batch_stride,
+                          o_batch_stride, scale, causal ? 1 : 0, causal ? q_pos_offset : 0,
+                          (cudaStream_t)stream);
+}
+
+size_t wattn_decode_workspace_bytes(int n_groups, int group_size, int t_kv, int n_heads) {
+  if (n_groups <= 0 || group_size <= 0 || t_kv <= 0 || n_heads <= 0) return 0;
+  // The f16/bf16 plan has the most splits; it bounds the f32 plan too.
+  const DecodePlan a = plan_decode(n_groups, group_size, t_kv, n_heads, WATTN_F16);
+  const DecodePlan b = plan_decode(n_groups, group_size, t_kv, n_heads, WATTN_F32);
+  return std::max(a.workspace_bytes, b.workspace_bytes);
+}
+
+int wattn_decode_fwd(const void *q, const void *k, const void *v, void *o, int q_dtype,
+                     int kv_dtype, int out_dtype, int n_groups, int group_size, int t_kv,
+                     int n_heads, int d_head, int64_t q_row_stride, int64_t kv_row_stride,
+                     int64_t kv_group_stride, int64_t o_row_stride, float scale, void *workspace,
+                     size_t workspace_bytes, void *stream) {
+  clear_error();
+  int rc = validate_decode(q, k, v, o, q_dtype, kv_dtype, out_dtype, n_groups, group_size, t_kv,
+                           n_heads, d_head, q_row_stride, kv_row_stride, kv_group_stride,
+                           o_row_stride, scale);
+  if (rc != WATTN_OK) return rc;
+  return decode_device(q, k, v, o, q_dtype, kv_dtype, out_dtype, n_groups, group_size, t_kv,
+                       n_heads, q_row_stride, kv_row_stride, kv_group_stride, o_row_stride, scale,
+                       workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int wattn_attention_host(const void *q, const void *k, const void *v, void *o, int in_dtype,
+                         int out_dtype, int batch, int t_q, int t_kv, int n_heads, float scale,
+                         int causal) {
+  clear_error();
+  return attention_host(q, k, v, o, in_dtype, out_dtype, batch, t_q, t_kv, n_heads, scale,
+                        causal ? 1 : 0, 0);
+}
+
+int wattn_decode_host(const void *q, const void *k, const void *v, void *o, int q_dtype,
+                      int kv_dtype, int out_dtype, int n_groups, int group_size, int t_kv,
+                      int n_heads, float scale) {
+  clear_error();
+  return decode_host(q, k, v, o, q_dtype, kv_dtype, out_dtype, n_groups, group_size, t_kv,
+                     n_heads, (int64_t)n_heads * kHeadDim, scale);
+}
+
+// ---- reference-signature mirrors (f32 host slices) -------------------------
+
+static int ref_shape(size_t n_heads, size_t d_model, int *d_head) {
+  // attention.rs:79-84 asserts n_heads > 0 and d_model % n_heads == 0.
+  if (n_heads == 0) return set_error(WATTN_ERR_INVALID, "n_heads must be non-zero");
+  if (d_model % n_heads != 0)
+    return set_error(WATTN_ERR_INVALID, "d_model (%zu) is not divisible by n_heads (%zu)", d_model,
+                     n_heads);
+  if (n_heads > 65535 || d_model > (1u << 24)) return set_error(WATTN_ERR_INVALID, "size too large");
+  *d_head = (int)(d_model / n_heads);
+  if (*d_head != kHeadDim)
+    return set_error(WATTN_ERR_UNSUPPORTED, "head dimension %d is not supported (64 only)", *d_head);
+  return WATTN_OK;
+}
+
+int wattn_flash_attention_2(const float *q, const float *k, const float *v, size_t t_q,
+                            size_t t_kv, size_t n_heads, size_t d_model, int causal,
+                            float *output) {
+  clear_error();
+  int d_head = 0;
+  int rc = ref_shape(n_heads, d_model, &d_head);
+  if (rc != WATTN_OK) return rc;
+  if (t_q > (size_t)INT32_MAX || t_kv > (size_t)INT32_MAX) return set_error(WATTN_ERR_INVALID, "size too large");
+  if (t_q == 0) return WATTN_OK;  // attention.rs:90-92
+  if (!q || !output || (t_kv > 0 && (!k || !v))) return set_error(WATTN_ERR_INVALID, "NULL slice");
+  if (t_kv == 0) {  // attention.rs:93-96
+    memset(output, 0, sizeof(float) * t_q * d_model);
+    return WATTN_OK;
+  }
+  if (t_q == 1 && !causal)  // attention.rs:102-104
+    return decode_host(q, k, v, output, WATTN_F32, WATTN_F32, WATTN_F32, 1, 1, (int)t_kv,
+                       (int)n_heads, (int64_t)d_model, 0.125f);
+  const float scale = 1.0f / sqrtf((float)d_head);  // attention.rs:107
+  return attention_host(q, k, v, output, WATTN_F32, WATTN_F32, 1, (int)t_q, (int)t_kv,
+                        (int)n_heads, scale, causal ? 1 : 0, 0);
+}
+
+int wattn_multi_head_attention(const float *q, const float *k, const float *v, size_t t_q,
+                               size_t t_kv, size_t n_heads, size_t d_model, int causal,
+                               float *output) {
+  return wattn_flash_attention_2(q, k, v, t_q, t_kv, n_heads, d_model, causal, output);
+}
+
+int wattn_single_token_mha_d64(const float *q, const float *k, const float *v, size_t t_kv,
+                               size_t n_heads, size_t d_model, float *output) {
+  clear_error();
+  if (n_heads == 0 || n_heads * kHeadDim != d_model)
+    return set_error(n_heads == 0 ? WATTN_ERR_INVALID : WATTN_ERR_UNSUPPORTED,
+                     "single_token_mha_d64 needs d_model == n_heads * 64");
+  if (t_kv > (size_t)INT32_MAX || n_heads > 65535) return set_error(WATTN_ERR_INVALID, "size too large");
+  if (!q || !output) return set_error(WATTN_ERR_INVALID, "NULL slice");
+  if (t_kv == 0) {
+    // softmax of an empty row leaves the accumulators at zero (attention.rs:355-388)
+    memset(output, 0, sizeof(float) * d_model);
+    return WATTN_OK;
+  }
+  if (!k || !v) return set_error(WATTN_ERR_INVALID, "NULL slice");
+  return decode_host(q, k, v, output, WATTN_F32, WATTN_F32, WATTN_F32, 1, 1, (int)t_kv,
+                     (int)n_heads, (int64_t)d_model, 0.125f);
+}
+
+int wattn_multi_head_attention_with_cache(const float *q, const float *k, const float *v,
+                                          size_t n_tokens, size_t total_tokens, size_t t_past,
+                                          size_t n_heads, size_t d_model, float *output) {
+  clear_error();
+  int d_head = 0;
+  int rc = ref_shape(n_heads, d_model, &d_head);
+  if (rc != WATTN_OK) return rc;
+  if (t_past + n_tokens > total_tokens)  // decoder.rs:848-849 (k.len() == total_tokens * d_model)
+    return set_error(WATTN_ERR_INVALID, "t_past + n_tokens exceeds total_tokens");
+  if (total_tokens > (size_t)INT32_MAX) return set_error(WATTN_ERR_INVALID, "size too large");
+  if (n_tokens == 0) return WATTN_OK;
+  if (!q || !k || !v || !output) return set_error(WATTN_ERR_INVALID, "NULL slice");
+  if (n_tokens == 1)  // decoder.rs:852-854: single_token_mha_d64 over t_past + 1 keys
+    return decode_host(q, k, v, output, WATTN_F32, WATTN_F32, WATTN_F32, 1, 1, (int)(t_past + 1),
+                       (int)n_heads, (int64_t)d_model, 0.125f);
+  const float scale = 1.0f / sqrtf((float)d_head);
+  return attention_host(q, k, v, output, WATTN_F32, WATTN_F32, 1, (int)n_tokens,
+                        (int)(t_past + n_tokens), (int)n_heads, scale, 1, (int)t_past);
+}
+
+int wattn_selftest_bounded_wait(int limit_us, void *stream) {
+  clear_error();
+  if (limit_us <= 0 || limit_us > 2000000)
+    return set_error(WATTN_ERR_INVALID, "limit_us must be in (0, 2e6]");
+  int *sp = device_status_ptr();
+  if (!sp) return WATTN_ERR_CUDA;
+  int *flag = nullptr;
+  if (cudaMalloc(&flag, sizeof(int)) != cudaSuccess) return check_launch("cudaMalloc(flag)");
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = WATTN_OK;
+  if (cudaMemsetAsync(flag, 0, sizeof(int), st) != cudaSuccess) rc = check_launch("memset flag");
+  if (rc == WATTN_OK) {
+    bounded_wait_kernel<<<1, 1, 0, st>>>(flag, sp, (unsigned long long)limit_us * 1000ull);
+    rc = check_launch("bounded_wait_kernel");
+  }
+  if (rc == WATTN_OK && cudaStreamSynchronize(st) != cudaSuccess) rc = check_launch("sync");
+  cudaFree(flag);
+  if (rc != WATTN_OK) return rc;
+  int s = WATTN_OK;
+  rc = wattn_device_status(-1, &s);
+  if (rc != WATTN_OK) return rc;
+  if (s != WATTN_OK) return set_error(s, "bounded wait ran out after %d us (as designed)", limit_us);
+  return WATTN_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,395 @@
+// attn_tc.cu -- encoder / general attention on the sm_100a tensor cores.
+//
+// Replaces the tiled online-softmax loop of flash_attention_2
+// (crates/tensor/src/ops/attention.rs:111-241) for f16 / bf16 inputs with
+// f32 accumulation. Same function, B200 structure:
+//
+//   * one CTA owns two 128-row query tiles of one (utterance, head); each
+//     tile has its own softmax warpgroup, so while one warpgroup turns S into
+//     P the tensor cores work on the other tile (ping-pong);
+//   * a TMA warp streams 128-key K and V tiles through a 3-deep ring in
+//     shared memory (128-byte swizzle, the layout UMMA reads directly);
+//   * an MMA warp issues tcgen05.mma: S = Q K^T (M=128, N=128, K=64) into
+//     tensor memory, then O += P V (M=128, N=64, K=128) with P read back from
+//     tensor memory;
+//   * the softmax warpgroup owns one query row per thread: it reads its S
+//     row from TMEM, keeps the running max m and normaliser l in registers
+//     (exp2 domain), rescales O in TMEM only when the max grows by more than
+//     2^8 (the result is exact either way: p never exceeds 256), and writes P
+//     as packed 16-bit pairs back to TMEM.
+//
+// Tensor memory per CTA (512 columns): tile t uses S at 256t (128 columns),
+// P at 256t+128 (64 columns of packed pairs), O at 256t+192 (64 columns).
+//
+// Reference semantics kept: ragged key tiles are masked (attention.rs:190-192),
+// causal rows see keys j <= i + q_pos_offset (:161-165; decoder.rs:864), the
+// output is acc / l with 0 for an empty row (:228-240). Head dim is 64.
+
+#include "wattn_common.cuh"
+#include "wattn_internal.h"
+
+namespace wattn {
+namespace {
+
+constexpr int kBM = 128;                 // query rows per tile (UMMA M)
+constexpr int kBN = 128;                 // keys per tile
+constexpr int kTiles = 2;                // query tiles per CTA
+constexpr int kStages = 3;               // K/V ring depth
+constexpr int kTileBytes = 128 * 128;    // 128 rows x 64 x 16-bit
+constexpr int kTmaWarp = 4 * kTiles;     // warp 8
+constexpr int kMmaWarp = kTmaWarp + 1;   // warp 9
+constexpr int kThreads = (kMmaWarp + 1) * 32;
+constexpr uint32_t kTmemCols = 512;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+struct Smem {
+  uint8_t q[kTiles][kTileBytes];
+  uint8_t k[kStages][kTileBytes];
+  uint8_t v[kStages][kTileBytes];
+  uint64_t q_full;
+  uint64_t k_full[kStages], k_empty[kStages];
+  uint64_t v_full[kStages], v_empty[kStages];
+  uint64_t s_full[kTiles];  // S(t, j) ready and PV(t, j-1) done; last phase: O final
+  uint64_t p_full[kTiles];  // P(t, j) in TMEM and O(t) rescaled
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+struct Params {
+  void *o;
+  int64_t o_rs, o_bs;
+  int t_q, t_kv;
+  float scale_log2;  // scale * log2(e)
+  int causal, q_pos_offset;
+  int *status;
+};
+
+template <typename OutT>
+WATTN_DEVINL void store_row(OutT *dst, const float *o, float inv) {
+  if constexpr (sizeof(OutT) == 4) {
+    float4 *d4 = reinterpret_cast<float4 *>(dst);
+#pragma unroll
+    for (int c = 0; c < 16; ++c)
+      d4[c] = make_float4(o[4 * c] * inv, o[4 * c + 1] * inv, o[4 * c + 2] * inv,
+                          o[4 * c + 3] * inv);
+  } else {
+    uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      uint4 w;
+      w.x = pack2<OutT>(o[8 * c + 0] * inv, o[8 * c + 1] * inv);
+      w.y = pack2<OutT>(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
+      w.z = pack2<OutT>(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
+      w.w = pack2<OutT>(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
+      d4[c] = w;
+    }
+  }
+}
+
+template <int IN_DT, int OUT_DT>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_q,
+                       const __grid_constant__ CUtensorMap map_k,
+                       const __grid_constant__ CUtensorMap map_v, const Params p) {
+  using InT = typename Elem<IN_DT>::T;
+  using OutT = typename Elem<OUT_DT>::T;
+  extern __shared__ uint8_t smem_raw[];
+  Smem &s = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                      ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int head = blockIdx.y, b = blockIdx.z;
+  const int q0 = blockIdx.x * (kBM * kTiles);
+  const int n_tiles = min(kTiles, (p.t_q - q0 + kBM - 1) / kBM);
+  int kv_end = p.t_kv;
+  if (p.causal) kv_end = min(kv_end, min(q0 + kBM * kTiles, p.t_q) + p.q_pos_offset);
+  const int nkv = kv_end > 0 ? (kv_end + kBN - 1) / kBN : 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&s.q_full, 1);
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&s.k_full[i], 1);
+      mbar_init(&s.k_empty[i], 1);
+      mbar_init(&s.v_full[i], 1);
+      mbar_init(&s.v_empty[i], 1);
+    }
+    for (int t = 0; t < kTiles; ++t) {
+      mbar_init(&s.s_full[t], 1);
+      mbar_init(&s.p_full[t], kBM);
+    }
+    mbar_init(&s.drain, 1);
+    s.abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(&s.tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+  volatile int *abort = &s.abort;
+
+  if (warp == kTmaWarp) {
+    // ---------------------------------------------------------- TMA producer
+    if (lane == 0 && nkv > 0) {
+      tma_prefetch_desc(&map_q);
+      tma_prefetch_desc(&map_k);
+      tma_prefetch_desc(&map_v);
+      mbar_arrive_expect_tx(&s.q_full, n_tiles * kTileBytes);
+      for (int t = 0; t < n_tiles; ++t)
+        tma_load_4d(s.q[t], &map_q, &s.q_full, 0, head, q0 + t * kBM, b);
+      int last_k = -1, last_v = -1;  // last tiles issued, for the wind-down
+      for (int j = 0; j < nkv; ++j) {
+        const int st = j % kStages;
+        const uint32_t ph = (j / kStages) & 1;
+        if (!mbar_wait(&s.k_empty[st], ph ^ 1, abort, p.status)) break;
+        mbar_arrive_expect_tx(&s.k_full[st], kTileBytes);
+        tma_load_4d(s.k[st], &map_k, &s.k_full[st], 0, head, j * kBN, b);
+        last_k = j;
+        if (!mbar_wait(&s.v_empty[st], ph ^ 1, abort, p.status)) break;
+        mbar_arrive_expect_tx(&s.v_full[st], kTileBytes);
+        tma_load_4d(s.v[st], &map_v, &s.v_full[st], 0, head, j * kBN, b);
+        last_v = j;
+      }
+      if (*abort) {
+        // Wind-down after a timeout: let the loads still in flight land
+        // before the CTA's shared memory is released (bounded waits).
+        volatile int no_abort = 0;
+        if (last_k >= 0)
+          mbar_wait(&s.k_full[last_k % kStages], (last_k / kStages) & 1, &no_abort, p.status);
+        if (last_v >= 0)
+          mbar_wait(&s.v_full[last_v % kStages], (last_v / kStages) & 1, &no_abort, p.status);
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0 && nkv > 0) {
+      constexpr uint32_t ab = IN_DT == WATTN_BF16 ? 1u : 0u;
+      constexpr uint32_t idesc_s = idesc_f16(ab, kBM, kBN, 0, 0);  // Q, K both K-major
+      constexpr uint32_t idesc_o = idesc_f16(ab, kBM, 64, 0, 1);   // P from TMEM, V MN-major
+      const uint32_t q_addr0 = smem_u32(s.q[0]);
+      const uint32_t k_addr0 = smem_u32(s.k[0]);
+      const uint32_t v_addr0 = smem_u32(s.v[0]);
+
+      auto issue_s = [&](int t, int st) {
+        const uint32_t qa = q_addr0 + t * kTileBytes, ka = k_addr0 + st * kTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)  // 4 x K=16 along the head dim
+          umma_ss(tmem + t * 256, smem_desc_sw128(qa + kk * 32, 16, 1024),
+                  smem_desc_sw128(ka + kk * 32, 16, 1024), idesc_s, kk > 0);
+      };
+      auto issue_pv = [&](int t, int st, bool acc) {
+        const uint32_t va = v_addr0 + st * kTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)  // 8 x K=16 along the keys
+          umma_ts(tmem + t * 256 + 192, tmem + t * 256 + 128 + kk * 8,
+                  smem_desc_sw128(va + kk * 2048, 16384, 1024), idesc_o, acc || kk > 0);
+      };
+
+      bool ok = mbar_wait(&s.q_full, 0, abort, p.status) &&
+                mbar_wait(&s.k_full[0], 0, abort, p.status);
+      if (ok) {
+        tc_fence_after();
+        for (int t = 0; t < n_tiles; ++t) {
+          issue_s(t, 0);
+          umma_commit(&s.s_full[t]);
+        }
+        umma_commit(&s.k_empty[0]);
+      }
+      for (int j = 0; ok && j < nkv; ++j) {
+        const int st = j % kStages;
+        const uint32_t ph = (j / kStages) & 1;
+        const int jn = j + 1, stn = jn % kStages;
+        const uint32_t phn = (jn / kStages) & 1;
+        if (!mbar_wait(&s.v_full[st], ph, abort, p.status)) break;
+        for (int t = 0; t < n_tiles; ++t) {
+          if (!mbar_wait(&s.p_full[t], j & 1, abort, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(t, st, j > 0);
+          if (t == n_tiles - 1) umma_commit(&s.v_empty[st]);
+          if (jn < nkv) {
+            if (t == 0 && !mbar_wait(&s.k_full[stn], phn, abort, p.status)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(t, stn);
+            if (t == n_tiles - 1) umma_commit(&s.k_empty[stn]);
+          }
+          umma_commit(&s.s_full[t]);
+        }
+      }
+      // Drain: every MMA issued above completes before TMEM is freed. This
+      // wait ignores `abort` (it must outlive a wind-down) but stays bounded.
+      volatile int no_abort = 0;
+      umma_commit(&s.drain);
+      mbar_wait(&s.drain, 0, &no_abort, p.status);
+    }
+  } else {
+    // ---------------------------------------------------------- softmax + epilogue
+    const int t = warp >> 2;   // query tile of this warpgroup
+    const int wq = warp & 3;   // TMEM lane quarter of this warp
+    const int row = wq * 32 + lane;
+    if (t < n_tiles && nkv > 0) {
+      const uint32_t lane_base = tmem + (uint32_t(wq * 32) << 16);
+      const uint32_t t_s = lane_base + t * 256;
+      const uint32_t t_p = t_s + 128, t_o = t_s + 192;
+      const int qrow = q0 + t * kBM + row;
+      const int key_lim = p.causal ? min(p.t_kv, qrow + p.q_pos_offset + 1) : p.t_kv;
+      const float c = p.scale_log2;
+      float m = -INFINITY, l = 0.f;
+      bool ok = true;
+      for (int j = 0; j < nkv; ++j) {
+        if (!mbar_wait(&s.s_full[t], j & 1, abort, p.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t r[4][32];
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) tmem_ld32(t_s + q4 * 32, r[q4]);
+        tmem_wait_ld();
+        float sv[128];
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) sv[q4 * 32 + i] = __uint_as_float(r[q4][i]);
+        const int lim = key_lim - j * kBN;
+        if (lim < kBN) {
+#pragma unroll
+          for (int i = 0; i < 128; ++i)
+            if (i >= lim) sv[i] = -INFINITY;
+        }
+        float mx = sv[0];
+#pragma unroll
+        for (int i = 1; i < 128; ++i) mx = fmaxf(mx, sv[i]);
+        const float mc = mx * c;
+        if (mc > m + kRescaleThreshold) {
+          const float alpha = ex2(m - mc);  // 0 on the first tile (m = -inf)
+          l *= alpha;
+          if (j > 0) {
+            uint32_t o[2][32];
+            tmem_ld32(t_o, o[0]);
+            tmem_ld32(t_o + 32, o[1]);
+            tmem_wait_ld();
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2)
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                o[h2][i] = __float_as_uint(__uint_as_float(o[h2][i]) * alpha);
+            tmem_st32(t_o, o[0]);
+            tmem_st32(t_o + 32, o[1]);
+          }
+          m = mc;
+        }
+        const float mu = (m == -INFINITY) ? 0.f : m;
+        uint32_t pk[2][32];
+        float lsum = 0.f;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          const float p0 = ex2(fmaf(sv[2 * i], c, -mu));
+          const float p1 = ex2(fmaf(sv[2 * i + 1], c, -mu));
+          lsum += p0 + p1;
+          pk[i >> 5][i & 31] = pack2<InT>(p0, p1);
+        }
+        l += lsum;
+        tmem_st32(t_p, pk[0]);
+        tmem_st32(t_p + 32, pk[1]);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&s.p_full[t]);
+      }
+      if (ok && mbar_wait(&s.s_full[t], nkv & 1, abort, p.status)) {
+        tc_fence_after();
+        uint32_t o[2][32];
+        tmem_ld32(t_o, o[0]);
+        tmem_ld32(t_o + 32, o[1]);
+        tmem_wait_ld();
+        if (qrow < p.t_q) {
+          float of[64];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            of[i] = __uint_as_float(o[0][i]);
+            of[32 + i] = __uint_as_float(o[1][i]);
+          }
+          const float inv = l > 0.f ? 1.f / l : 0.f;
+          OutT *dst = reinterpret_cast<OutT *>(p.o) + (int64_t)b * p.o_bs +
+                      (int64_t)qrow * p.o_rs + head * kHeadDim;
+          store_row<OutT>(dst, of, inv);
+        }
+      }
+    }
+  }
+
+  // Teardown: after the last TMEM access of every warp, free the columns.
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+template <int IN_DT, int OUT_DT>
+int launch_typed(const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &mv,
+                 const Params &p, int batch, int n_heads, cudaStream_t stream) {
+  auto kern = attn_fwd_tc_kernel<IN_DT, OUT_DT>;
+  const int smem = (int)sizeof(Smem) + 1024;
+  // Per device and idempotent; cheap enough to repeat on every launch.
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+      cudaSuccess)
+    return check_launch("cudaFuncSetAttribute(attn_fwd_tc)");
+  dim3 grid((p.t_q + kBM * kTiles - 1) / (kBM * kTiles), n_heads, batch);
+  kern<<<grid, kThreads, smem, stream>>>(mq, mk, mv, p);
+  return check_launch("attn_fwd_tc");
+}
+
+int make_qkv_map(CUtensorMap *map, const void *base, int dt, int n_heads, int t, int batch,
+                 int64_t rs, int64_t bs) {
+  const uint64_t es = elem_size(dt);
+  const uint64_t dims[4] = {64, (uint64_t)n_heads, (uint64_t)t, (uint64_t)batch};
+  const uint64_t strides[3] = {64 * es, (uint64_t)rs * es,
+                               (uint64_t)(batch > 1 ? bs : (int64_t)t * rs) * es};
+  const uint32_t box[4] = {64, 1, kBM, 1};
+  return encode_tmap(map, tmap_dtype(dt), 4, base, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+}  // namespace
+
+int launch_attn_tc(const void *q, const void *k, const void *v, void *o, int in_dtype,
+                   int out_dtype, int batch, int t_q, int t_kv, int n_heads, int64_t q_rs,
+                   int64_t kv_rs, int64_t o_rs, int64_t q_bs, int64_t kv_bs, int64_t o_bs,
+                   float scale, int causal, int q_pos_offset, cudaStream_t stream) {
+  CUtensorMap mq, mk, mv;
+  int rc;
+  if ((rc = make_qkv_map(&mq, q, in_dtype, n_heads, t_q, batch, q_rs, q_bs)) != WATTN_OK) return rc;
+  if ((rc = make_qkv_map(&mk, k, in_dtype, n_heads, t_kv, batch, kv_rs, kv_bs)) != WATTN_OK) return rc;
+  if ((rc = make_qkv_map(&mv, v, in_dtype, n_heads, t_kv, batch, kv_rs, kv_bs)) != WATTN_OK) return rc;
+  Params p;
+  p.o = o;
+  p.o_rs = o_rs;
+  p.o_bs = o_bs;
+  p.t_q = t_q;
+  p.t_kv = t_kv;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.causal = causal;
+  p.q_pos_offset = q_pos_offset;
+  p.status = device_status_ptr();
+  if (p.status == nullptr) return WATTN_ERR_CUDA;
+  if (in_dtype == WATTN_F16) {
+    if (out_dtype == WATTN_F32)
+      return launch_typed<WATTN_F16, WATTN_F32>(mq, mk, mv, p, batch, n_heads, stream);
+    return launch_typed<WATTN_F16, WATTN_F16>(mq, mk, mv, p, batch, n_heads, stream);
+  }
+  if (out_dtype == WATTN_F32)
+    return launch_typed<WATTN_BF16, WATTN_F32>(mq, mk, mv, p, batch, n_heads, stream);
+  return launch_typed<WATTN_BF16, WATTN_BF16>(mq, mk, mv, p, batch, n_heads, stream);
+}
+
+}  // namespace wattn

@@ -1,0 +1,100 @@
+// wattn_internal.h -- host-side declarations shared by the library's .cu files.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/wattn.h"
+
+namespace wattn {
+
+// Records `msg` (printf-style) as the calling thread's last error and
+// returns `status`.
+int set_error(int status, const char *fmt, ...);
+void clear_error();
+
+// Status word of the current device (device address), for kernel params.
+int *device_status_ptr();
+
+// cuTensorMapEncodeTiled, resolved once through the runtime's driver entry
+// point (no link-time dependency on libcuda).
+int encode_tmap(CUtensorMap *map, CUtensorMapDataType dtype, uint32_t rank, const void *base,
+                const uint64_t *dims, const uint64_t *strides_bytes, const uint32_t *box,
+                CUtensorMapSwizzle swizzle);
+
+inline int elem_size(int dt) { return dt == WATTN_F32 ? 4 : 2; }
+inline bool valid_dtype(int dt) { return dt == WATTN_F32 || dt == WATTN_F16 || dt == WATTN_BF16; }
+inline CUtensorMapDataType tmap_dtype(int dt) {
+  return dt == WATTN_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+         : dt == WATTN_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                           : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+}
+
+// Checks the last CUDA error after a launch; returns WATTN_OK or WATTN_ERR_CUDA.
+int check_launch(const char *what);
+
+// ----------------------------------------------------------- kernel launchers
+// All pointers device, strides in elements; arguments already validated.
+
+// tcgen05 tensor-core attention, 16-bit inputs (attn_tc.cu).
+int launch_attn_tc(const void *q, const void *k, const void *v, void *o, int in_dtype,
+                   int out_dtype, int batch, int t_q, int t_kv, int n_heads, int64_t q_rs,
+                   int64_t kv_rs, int64_t o_rs, int64_t q_bs, int64_t kv_bs, int64_t o_bs,
+                   float scale, int causal, int q_pos_offset, cudaStream_t stream);
+
+// f32 CUDA-core attention (attn_f32.cu).
+int launch_attn_f32(const float *q, const float *k, const float *v, float *o, int batch,
+                    int t_q, int t_kv, int n_heads, int64_t q_rs, int64_t kv_rs, int64_t o_rs,
+                    int64_t q_bs, int64_t kv_bs, int64_t o_bs, float scale, int causal,
+                    int q_pos_offset, cudaStream_t stream);
+
+// Zero-fills a strided [batch][t][n_heads*64] output (t_kv == 0 case).
+int launch_zero_rows(void *o, int out_dtype, int batch, int t, int width, int64_t o_rs,
+                     int64_t o_bs, cudaStream_t stream);
+
+// Split-KV decode over dense K/V (decode.cu).
+struct DecodePlan {
+  int chunk;      // keys per split (multiple of 64)
+  int n_splits;   // splits per (row chunk, head)
+  int row_chunks; // ceil(group_size / rows per CTA)
+  size_t workspace_bytes;
+};
+DecodePlan plan_decode(int n_groups, int group_size, int t_kv, int n_heads, int kv_dtype);
+int launch_decode(const void *q, const void *k, const void *v, void *o, int q_dtype,
+                  int kv_dtype, int out_dtype, int n_groups, int group_size, int t_kv,
+                  int n_heads, int64_t q_rs, int64_t kv_rs, int64_t kv_gs, int64_t o_rs,
+                  float scale, void *workspace, size_t workspace_bytes, cudaStream_t stream);
+
+// ----------------------------------------------------------- paged decode
+constexpr int kDecSubRows = 64;     // keys per decode sub-tile (TMA box rows)
+constexpr int kPagedMaxRows = 256;  // query rows per paged launch
+constexpr int kPagedMaxPages = 16;  // pages per row in one launch
+
+// Kernel-parameter table of one paged decode launch (passed by value, about
+// 18 KB): for each query row, its slot's pages and the physical key range
+// [kv_lo, kv_hi) it attends.
+struct PagedTable {
+  int n_rows;
+  int layer, n_layers, page_rows;
+  int kv_lo[kPagedMaxRows];
+  int kv_hi[kPagedMaxRows];
+  int pages[kPagedMaxRows][kPagedMaxPages];
+};
+
+// `map_k` / `map_v` view the page pool as 2-D [rows][64] (box 64 rows).
+int launch_decode_paged(const CUtensorMap &map_k, const CUtensorMap &map_v, const void *q,
+                        void *o, int q_dtype, int kv_dtype, int out_dtype, int n_heads,
+                        int64_t q_rs, int64_t o_rs, float scale, const PagedTable &pt,
+                        int max_keys, void *workspace, size_t workspace_bytes,
+                        cudaStream_t stream);
+// Upper bound of the workspace of a paged launch of n_rows rows whose key
+// ranges span at most max_keys rows.
+size_t paged_workspace_bytes(int n_rows, int n_heads, int max_keys);
+
+// Library-owned, zero-initialised decode workspace of the calling thread on
+// the current device (grown on demand). Returns NULL on allocation failure.
+void *thread_workspace(size_t bytes, cudaStream_t stream);
+
+}  // namespace wattn
