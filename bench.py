@@ -103,7 +103,11 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.monotonic(), line.strip()))
+
+    def mark(self):
+        """Called at the start and at the end of the timed region."""
+        self.marks = getattr(self, "marks", []) + [time.monotonic()]
 
     def __exit__(self, *a):
         if self.proc is not None:
@@ -116,7 +120,14 @@ class ClockSampler:
     def summary(self) -> dict:
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        marks = getattr(self, "marks", [])
+        lines = self.lines
+        if len(marks) >= 2:  # keep the samples taken inside the timed region
+            inside = [ln for t, ln in lines if marks[0] <= t <= marks[1]]
+            lines = inside or [ln for _, ln in lines[-3:]]
+        else:
+            lines = [ln for _, ln in lines]
+        for ln in lines:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -200,14 +211,16 @@ def bench_encoder(W, rank, world, steps, warmup, e2e_steps):
         W.attention_fwd(q, k, v, o, batch=bl, t_q=T, t_kv=T, n_heads=H, scale=0.125,
                         stream=stream)
 
-    for _ in range(warmup):
-        for i in range(L):
-            run_layer(i)
-    barrier(world)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(steps * L)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(torch.cuda.current_device()) as clk:
+        # the sampler starts during warm-up so that it is sampling when timing starts
+        for _ in range(warmup):
+            for i in range(L):
+                run_layer(i)
+        barrier(world)
+        clk.mark()
         start.record(stream)
         for s in range(steps):
             for i in range(L):
@@ -217,6 +230,7 @@ def bench_encoder(W, rank, world, steps, warmup, e2e_steps):
                 e1.record(stream)
         end.record(stream)
         torch.cuda.synchronize()
+        clk.mark()
     barrier(world)
     ms_local = start.elapsed_time(end)
     ms = max_over_ranks(ms_local, world)

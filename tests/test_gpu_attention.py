@@ -10,7 +10,7 @@ import os
 import numpy as np
 import pytest
 
-from tests.helpers import (TOL_F32_MAXABS, check_16bit, check_f32, randn, rounded)
+from tests.helpers import (TOL_F32_MAXABS, check_16bit, check_f32, half_ulp, randn, rounded)
 
 pytestmark = pytest.mark.gpu
 
@@ -50,7 +50,7 @@ def test_tc_kat_shapes(W, oracle, dt, shape):
     ref = oracle.flash_attention_2(qf, kf, vf, t_q, t_kv, h, h * 64, causal)
     for out_dt in (0, dt):
         out = _run_fwd(W, qd, kd, vd, out_dt, 1, t_q, t_kv, h, causal)
-        check_16bit(out, ref, f"{shape} dt={dt} out={out_dt}")
+        check_16bit(out, ref, f"{shape} dt={dt} out={out_dt}", out_dt)
 
 
 @pytest.mark.parametrize("dt", [1, 2], ids=["f16", "bf16"])
@@ -64,7 +64,7 @@ def test_tc_whisper_shapes(W, oracle, dt, cfg):
                                     for s, t in ((11, t_q), (12, t_kv), (13, t_kv)))
     ref = oracle.flash_attention_2_batched(qf, kf, vf, b, t_q, t_kv, h, d, False)
     out = _run_fwd(W, qd, kd, vd, dt, b, t_q, t_kv, h)
-    check_16bit(out, ref, f"{cfg}")
+    check_16bit(out, ref, f"{cfg}", dt)
 
 
 def test_tc_fused_qkv_buffer(W, oracle):
@@ -224,7 +224,7 @@ def test_full_size_large_v3_layer(W, oracle):
         sl = slice(u * t * d, (u + 1) * t * d)
         ref = oracle.flash_attention_2(q[sl].float().numpy(), k[sl].float().numpy(),
                                        v[sl].float().numpy(), t, t, h, d, False)
-        check_16bit(out[u], ref, f"utterance {u}")
+        check_16bit(out[u], ref, f"utterance {u}", 2)
     u = 5
     perm = torch.randperm(t, generator=g)
     k2 = kd.view(b, t, d).clone()
@@ -237,4 +237,4 @@ def test_full_size_large_v3_layer(W, oracle):
     torch.cuda.synchronize()
     a = o.view(b, t * d)[u].float().cpu().numpy()
     c = o2.view(b, t * d)[u].float().cpu().numpy()
-    assert np.abs(a - c).max() <= 2e-3
+    assert np.abs(a - c).max() <= 2e-3 + 2 * half_ulp(a, 2).max()

@@ -16,7 +16,8 @@
 
 namespace wattn {
 
-__device__ int g_status = WATTN_OK;
+// [0] status word, [1] site of the first bounded wait that ran out.
+__device__ int g_status[2] = {WATTN_OK, 0};
 
 namespace {
 
@@ -153,7 +154,7 @@ __global__ void bounded_wait_kernel(volatile int *flag, int *status,
   const unsigned long long t0 = globaltimer_ns();
   while (*flag == 0) {
     if (globaltimer_ns() - t0 > limit_ns) {
-      report_timeout(status);
+      report_timeout(status, (9 << 24));
       return;
     }
     __nanosleep(1000);
@@ -230,12 +231,12 @@ int finish_host(HostCtx *h, int rc) {
       rc = check_launch("cudaStreamSynchronize");
   if (rc != WATTN_OK) return rc;
   int *sp = device_status_ptr();
-  int s = WATTN_OK;
-  if (sp && cudaMemcpy(&s, sp, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess &&
-      s != WATTN_OK) {
-    const int zero = WATTN_OK;
-    cudaMemcpy(sp, &zero, sizeof(int), cudaMemcpyHostToDevice);
-    return set_error(s, "a kernel's bounded wait ran out");
+  int s[2] = {WATTN_OK, 0};
+  if (sp && cudaMemcpy(s, sp, sizeof(s), cudaMemcpyDeviceToHost) == cudaSuccess &&
+      s[0] != WATTN_OK) {
+    const int zero[2] = {WATTN_OK, 0};
+    cudaMemcpy(sp, zero, sizeof(zero), cudaMemcpyHostToDevice);
+    return set_error(s[0], "a kernel's bounded wait ran out (site 0x%08x)", s[1]);
   }
   return WATTN_OK;
 }
@@ -495,14 +496,16 @@ int wattn_device_status(int device, int *status) {
   int *sp = device_status_ptr();
   if (!sp) rc = WATTN_ERR_CUDA;
   if (rc == WATTN_OK && cudaDeviceSynchronize() != cudaSuccess) rc = check_launch("cudaDeviceSynchronize");
-  int s = WATTN_OK;
-  if (rc == WATTN_OK && cudaMemcpy(&s, sp, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+  int s[2] = {WATTN_OK, 0};
+  if (rc == WATTN_OK && cudaMemcpy(s, sp, sizeof(s), cudaMemcpyDeviceToHost) != cudaSuccess)
     rc = check_launch("read status word");
-  const int zero = WATTN_OK;
-  if (rc == WATTN_OK && cudaMemcpy(sp, &zero, sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess)
+  const int zero[2] = {WATTN_OK, 0};
+  if (rc == WATTN_OK && cudaMemcpy(sp, zero, sizeof(zero), cudaMemcpyHostToDevice) != cudaSuccess)
     rc = check_launch("clear status word");
   if (device >= 0 && device != prev) cudaSetDevice(prev);
-  *status = s;
+  *status = s[0];
+  if (rc == WATTN_OK && s[0] != WATTN_OK)
+    set_error(s[0], "bounded wait ran out at site 0x%08x", s[1]);
   return rc;
 }
 

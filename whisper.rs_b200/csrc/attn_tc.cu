@@ -56,6 +56,9 @@ struct Smem {
   int abort;
 };
 
+// Wait sites (kernel 1): role << 16 | barrier << 8 | iteration.
+#define TC_SITE(role, bar, j) ((1 << 24) | ((role) << 16) | ((bar) << 8) | ((j) & 0xff))
+
 struct Params {
   void *o;
   int64_t o_rs, o_bs;
@@ -63,6 +66,9 @@ struct Params {
   float scale_log2;  // scale * log2(e)
   int causal, q_pos_offset;
   int *status;
+#ifdef WATTN_TC_DEBUG
+  float *dbg;  // debug builds only: S, P of key tile 0, raw O and l per row
+#endif
 };
 
 template <typename OutT>
@@ -122,6 +128,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_barrier_init();
   }
   if (warp == kMmaWarp) {
+    __syncwarp();
     tmem_alloc(&s.tmem_base, kTmemCols);
     tmem_relinquish();
   }
@@ -144,11 +151,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < nkv; ++j) {
         const int st = j % kStages;
         const uint32_t ph = (j / kStages) & 1;
-        if (!mbar_wait(&s.k_empty[st], ph ^ 1, abort, p.status)) break;
+        if (!mbar_wait(&s.k_empty[st], ph ^ 1, abort, p.status, TC_SITE(1, 1, j))) break;
         mbar_arrive_expect_tx(&s.k_full[st], kTileBytes);
         tma_load_4d(s.k[st], &map_k, &s.k_full[st], 0, head, j * kBN, b);
         last_k = j;
-        if (!mbar_wait(&s.v_empty[st], ph ^ 1, abort, p.status)) break;
+        if (!mbar_wait(&s.v_empty[st], ph ^ 1, abort, p.status, TC_SITE(1, 2, j))) break;
         mbar_arrive_expect_tx(&s.v_full[st], kTileBytes);
         tma_load_4d(s.v[st], &map_v, &s.v_full[st], 0, head, j * kBN, b);
         last_v = j;
@@ -158,9 +165,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         // before the CTA's shared memory is released (bounded waits).
         volatile int no_abort = 0;
         if (last_k >= 0)
-          mbar_wait(&s.k_full[last_k % kStages], (last_k / kStages) & 1, &no_abort, p.status);
+          mbar_wait(&s.k_full[last_k % kStages], (last_k / kStages) & 1, &no_abort, p.status,
+                    TC_SITE(1, 3, last_k));
         if (last_v >= 0)
-          mbar_wait(&s.v_full[last_v % kStages], (last_v / kStages) & 1, &no_abort, p.status);
+          mbar_wait(&s.v_full[last_v % kStages], (last_v / kStages) & 1, &no_abort, p.status,
+                    TC_SITE(1, 4, last_v));
       }
     }
   } else if (warp == kMmaWarp) {
@@ -188,8 +197,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                   smem_desc_sw128(va + kk * 2048, 16384, 1024), idesc_o, acc || kk > 0);
       };
 
-      bool ok = mbar_wait(&s.q_full, 0, abort, p.status) &&
-                mbar_wait(&s.k_full[0], 0, abort, p.status);
+      bool ok = mbar_wait(&s.q_full, 0, abort, p.status, TC_SITE(2, 0, 0)) &&
+                mbar_wait(&s.k_full[0], 0, abort, p.status, TC_SITE(2, 1, 0));
       if (ok) {
         tc_fence_after();
         for (int t = 0; t < n_tiles; ++t) {
@@ -203,9 +212,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t ph = (j / kStages) & 1;
         const int jn = j + 1, stn = jn % kStages;
         const uint32_t phn = (jn / kStages) & 1;
-        if (!mbar_wait(&s.v_full[st], ph, abort, p.status)) break;
+        if (!mbar_wait(&s.v_full[st], ph, abort, p.status, TC_SITE(2, 2, j))) break;
         for (int t = 0; t < n_tiles; ++t) {
-          if (!mbar_wait(&s.p_full[t], j & 1, abort, p.status)) {
+          if (!mbar_wait(&s.p_full[t], j & 1, abort, p.status, TC_SITE(2, 3 + t, j))) {
             ok = false;
             break;
           }
@@ -213,7 +222,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           issue_pv(t, st, j > 0);
           if (t == n_tiles - 1) umma_commit(&s.v_empty[st]);
           if (jn < nkv) {
-            if (t == 0 && !mbar_wait(&s.k_full[stn], phn, abort, p.status)) {
+            if (t == 0 && !mbar_wait(&s.k_full[stn], phn, abort, p.status, TC_SITE(2, 5, jn))) {
               ok = false;
               break;
             }
@@ -228,7 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // wait ignores `abort` (it must outlive a wind-down) but stays bounded.
       volatile int no_abort = 0;
       umma_commit(&s.drain);
-      mbar_wait(&s.drain, 0, &no_abort, p.status);
+      mbar_wait(&s.drain, 0, &no_abort, p.status, TC_SITE(2, 6, 0));
     }
   } else {
     // ---------------------------------------------------------- softmax + epilogue
@@ -245,7 +254,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       float m = -INFINITY, l = 0.f;
       bool ok = true;
       for (int j = 0; j < nkv; ++j) {
-        if (!mbar_wait(&s.s_full[t], j & 1, abort, p.status)) {
+        const bool got = mbar_wait(&s.s_full[t], j & 1, abort, p.status, TC_SITE(3 + t, 0, j));
+        // The whole warp takes the same branch and is converged before the
+        // .sync.aligned TMEM accesses below.
+        if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;
         }
@@ -254,11 +266,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) tmem_ld32(t_s + q4 * 32, r[q4]);
         tmem_wait_ld();
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) reg_fence(r[q4]);
         float sv[128];
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4)
 #pragma unroll
           for (int i = 0; i < 32; ++i) sv[q4 * 32 + i] = __uint_as_float(r[q4][i]);
+#ifdef WATTN_TC_DEBUG
+        if (p.dbg && j == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
+          for (int i = 0; i < 128; ++i) p.dbg[(t * 128 + row) * 128 + i] = sv[i];
+#endif
         const int lim = key_lim - j * kBN;
         if (lim < kBN) {
 #pragma unroll
@@ -269,14 +287,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 1; i < 128; ++i) mx = fmaxf(mx, sv[i]);
         const float mc = mx * c;
-        if (mc > m + kRescaleThreshold) {
-          const float alpha = ex2(m - mc);  // 0 on the first tile (m = -inf)
+        // Lazy rescale. The TMEM accesses below are .sync.aligned, so the
+        // branch is taken by the whole warp whenever any lane needs it;
+        // lanes that do not need it rescale by 1.
+        const bool need = mc > m + kRescaleThreshold;
+        if (__any_sync(0xffffffffu, need)) {
+          const float alpha = need ? ex2(m - mc) : 1.f;  // 0 on the first tile (m = -inf)
           l *= alpha;
           if (j > 0) {
             uint32_t o[2][32];
             tmem_ld32(t_o, o[0]);
             tmem_ld32(t_o + 32, o[1]);
             tmem_wait_ld();
+            reg_fence(o[0]);
+            reg_fence(o[1]);
 #pragma unroll
             for (int h2 = 0; h2 < 2; ++h2)
 #pragma unroll
@@ -285,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_st32(t_o, o[0]);
             tmem_st32(t_o + 32, o[1]);
           }
-          m = mc;
+          if (need) m = mc;
         }
         const float mu = (m == -INFINITY) ? 0.f : m;
         uint32_t pk[2][32];
@@ -294,22 +318,44 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 64; ++i) {
           const float p0 = ex2(fmaf(sv[2 * i], c, -mu));
           const float p1 = ex2(fmaf(sv[2 * i + 1], c, -mu));
-          lsum += p0 + p1;
-          pk[i >> 5][i & 31] = pack2<InT>(p0, p1);
+          const uint32_t w = pack2<InT>(p0, p1);
+          pk[i >> 5][i & 31] = w;
+          // Normalise by the sum of the rounded weights the tensor core
+          // multiplies V with: the weights then sum to exactly one and the
+          // rounding error of a dominant weight cancels in acc / l.
+          const float2 r2 = unpack2<InT>(w);
+          lsum += r2.x + r2.y;
         }
         l += lsum;
+#ifdef WATTN_TC_DEBUG
+        if (p.dbg && j == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
+          for (int i = 0; i < 128; ++i)
+            p.dbg[32768 + (t * 128 + row) * 128 + i] = ex2(fmaf(sv[i], c, -mu));
+#endif
         tmem_st32(t_p, pk[0]);
         tmem_st32(t_p + 32, pk[1]);
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&s.p_full[t]);
       }
-      if (ok && mbar_wait(&s.s_full[t], nkv & 1, abort, p.status)) {
+      const bool fin = ok && mbar_wait(&s.s_full[t], nkv & 1, abort, p.status, TC_SITE(3 + t, 1, nkv));
+      if (__all_sync(0xffffffffu, fin)) {
         tc_fence_after();
         uint32_t o[2][32];
         tmem_ld32(t_o, o[0]);
         tmem_ld32(t_o + 32, o[1]);
         tmem_wait_ld();
+        reg_fence(o[0]);
+        reg_fence(o[1]);
+#ifdef WATTN_TC_DEBUG
+        if (p.dbg && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) {
+          for (int i = 0; i < 32; ++i) {
+            p.dbg[65536 + (t * 128 + row) * 64 + i] = __uint_as_float(o[0][i]);
+            p.dbg[65536 + (t * 128 + row) * 64 + 32 + i] = __uint_as_float(o[1][i]);
+          }
+          p.dbg[65536 + 16384 + t * 128 + row] = l;
+        }
+#endif
         if (qrow < p.t_q) {
           float of[64];
 #pragma unroll
@@ -330,6 +376,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == kMmaWarp) {
+    __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
@@ -362,6 +409,11 @@ int make_qkv_map(CUtensorMap *map, const void *base, int dt, int n_heads, int t,
 
 }  // namespace
 
+#ifdef WATTN_TC_DEBUG
+float *g_tc_dbg = nullptr;
+extern "C" void wattn_debug_set_tc_dump(float *p) { g_tc_dbg = p; }
+#endif
+
 int launch_attn_tc(const void *q, const void *k, const void *v, void *o, int in_dtype,
                    int out_dtype, int batch, int t_q, int t_kv, int n_heads, int64_t q_rs,
                    int64_t kv_rs, int64_t o_rs, int64_t q_bs, int64_t kv_bs, int64_t o_bs,
@@ -382,6 +434,9 @@ int launch_attn_tc(const void *q, const void *k, const void *v, void *o, int in_
   p.q_pos_offset = q_pos_offset;
   p.status = device_status_ptr();
   if (p.status == nullptr) return WATTN_ERR_CUDA;
+#ifdef WATTN_TC_DEBUG
+  p.dbg = g_tc_dbg;
+#endif
   if (in_dtype == WATTN_F16) {
     if (out_dtype == WATTN_F32)
       return launch_typed<WATTN_F16, WATTN_F32>(mq, mk, mv, p, batch, n_heads, stream);

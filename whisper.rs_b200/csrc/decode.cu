@@ -34,6 +34,11 @@ constexpr int kDecRows = 8;        // query rows per CTA
 constexpr int kDecThreads = 128;
 constexpr int kDecMaxSubs = 4;     // sub-tiles per split (chunk <= 256 keys; 128 for f32)
 constexpr int kPartStride = 66;    // floats per partial: acc[64], m, l
+// Workspace layout, the same for every call: [counters][partials]. The
+// counter region has a fixed size, so partials written by one call can never
+// land where a later call of another shape keeps its counters; every call
+// leaves the counters it used at zero.
+constexpr size_t kCounterBytes = (size_t)kMaxSplitCounters * sizeof(int);
 static_assert(kDecSub == kDecSubRows, "paged sub-tiles and TMA boxes must agree");
 
 namespace {
@@ -232,7 +237,7 @@ __device__ void decode_body(const CUtensorMap &map_k, const CUtensorMap &map_v,
   // ---- scores: warp w takes keys 16w.. of every sub-tile, two lanes per key
   const int krow = warp * 16 + (lane >> 1), half = lane & 1;
   for (int st = 0; st < n_sub; ++st) {
-    mbar_wait(&s.kbar[st], 0, abort, p.status);
+    mbar_wait(&s.kbar[st], 0, abort, p.status, (2 << 24) | (1 << 16) | (st << 8));
     float dot[kDecRows];
     half_dots<KV_DT>(s.k[st], krow, half, s.q, nr, dot);
     const int key = k_beg + st * kDecSub + krow;
@@ -272,7 +277,7 @@ __device__ void decode_body(const CUtensorMap &map_k, const CUtensorMap &map_v,
 #pragma unroll
   for (int r = 0; r < kDecRows; ++r) acc[r][0] = acc[r][1] = 0.f;
   for (int st = 0; st < n_sub; ++st) {
-    mbar_wait(&s.vbar[st], 0, abort, p.status);
+    mbar_wait(&s.vbar[st], 0, abort, p.status, (2 << 24) | (2 << 16) | (st << 8));
 #pragma unroll 4
     for (int kk = 0; kk < 16; ++kk) {
       const int vrow = warp * 16 + kk;
@@ -442,8 +447,7 @@ DecodePlan plan_decode(int n_groups, int group_size, int t_kv, int n_heads, int 
   pl.chunk = chunk_for(kv_dtype, n_groups * pl.row_chunks * n_heads, t_kv);
   pl.n_splits = t_kv > 0 ? (t_kv + pl.chunk - 1) / pl.chunk : 1;
   const size_t rows = (size_t)n_groups * group_size;
-  pl.workspace_bytes = align256(rows * n_heads * pl.n_splits * kPartStride * sizeof(float)) +
-                       align256((size_t)n_groups * pl.row_chunks * n_heads * sizeof(int));
+  pl.workspace_bytes = kCounterBytes + rows * n_heads * pl.n_splits * kPartStride * sizeof(float);
   return pl;
 }
 
@@ -455,6 +459,9 @@ int launch_decode(const void *q, const void *k, const void *v, void *o, int q_dt
   if (pl.n_splits > 1 && workspace_bytes < pl.workspace_bytes)
     return set_error(WATTN_ERR_INVALID, "decode: workspace of %zu bytes, %zu needed",
                      workspace_bytes, pl.workspace_bytes);
+  if ((size_t)n_groups * pl.row_chunks * n_heads > (size_t)kMaxSplitCounters)
+    return set_error(WATTN_ERR_INVALID, "decode: %d row groups x %d heads exceed %d per call",
+                     n_groups * pl.row_chunks, n_heads, kMaxSplitCounters);
   const uint64_t es = elem_size(kv_dtype);
   const uint64_t dims[4] = {64, (uint64_t)n_heads, (uint64_t)t_kv, (uint64_t)n_groups};
   const uint64_t strides[3] = {64 * es, (uint64_t)kv_rs * es,
@@ -479,10 +486,8 @@ int launch_decode(const void *q, const void *k, const void *v, void *o, int q_dt
   p.n_splits = pl.n_splits;
   p.chunk = pl.chunk;
   p.scale_log2 = scale * 1.4426950408889634f;
-  const size_t part_bytes =
-      align256((size_t)n_groups * group_size * n_heads * pl.n_splits * kPartStride * sizeof(float));
-  p.part = reinterpret_cast<float *>(workspace);
-  p.count = reinterpret_cast<int *>(reinterpret_cast<uint8_t *>(workspace) + part_bytes);
+  p.count = reinterpret_cast<int *>(workspace);
+  p.part = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(workspace) + kCounterBytes);
   p.status = device_status_ptr();
   if (p.status == nullptr) return WATTN_ERR_CUDA;
   return dispatch<false>(q_dtype, kv_dtype, out_dtype, mk, mv, p, n_groups, nullptr, 0, stream);
@@ -506,16 +511,17 @@ int launch_decode_paged(const CUtensorMap &map_k, const CUtensorMap &map_v, cons
   p.chunk = chunk_for(kv_dtype, pt.n_rows * n_heads, max_keys);
   p.n_splits = (max_keys + p.chunk - 1) / p.chunk;  // upper bound; rows use their own
   p.scale_log2 = scale * 1.4426950408889634f;
-  const size_t part_bytes =
-      align256((size_t)pt.n_rows * n_heads * p.n_splits * kPartStride * sizeof(float));
-  const size_t need = part_bytes + align256((size_t)pt.n_rows * n_heads * sizeof(int));
+  const size_t need =
+      kCounterBytes + (size_t)pt.n_rows * n_heads * p.n_splits * kPartStride * sizeof(float);
   if (need > paged_workspace_bytes(pt.n_rows, n_heads, max_keys))
     return set_error(WATTN_ERR_INVALID, "paged decode: internal workspace bound violated");
+  if ((size_t)pt.n_rows * n_heads > (size_t)kMaxSplitCounters)
+    return set_error(WATTN_ERR_INVALID, "paged decode: too many rows x heads per launch");
   if (workspace_bytes < need)
     return set_error(WATTN_ERR_INVALID, "paged decode: workspace of %zu bytes, %zu needed",
                      workspace_bytes, need);
-  p.part = reinterpret_cast<float *>(workspace);
-  p.count = reinterpret_cast<int *>(reinterpret_cast<uint8_t *>(workspace) + part_bytes);
+  p.count = reinterpret_cast<int *>(workspace);
+  p.part = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(workspace) + kCounterBytes);
   p.status = device_status_ptr();
   if (p.status == nullptr) return WATTN_ERR_CUDA;
   return dispatch<true>(q_dtype, kv_dtype, out_dtype, map_k, map_v, p, 0, &pt, p.n_splits,
@@ -525,8 +531,7 @@ int launch_decode_paged(const CUtensorMap &map_k, const CUtensorMap &map_v, cons
 size_t paged_workspace_bytes(int n_rows, int n_heads, int max_keys) {
   // Every chunk is at least one sub-tile, so splits <= ceil(max_keys / 64).
   const int n_splits = (max_keys + kDecSub - 1) / kDecSub;
-  return align256((size_t)n_rows * n_heads * n_splits * kPartStride * sizeof(float)) +
-         align256((size_t)n_rows * n_heads * sizeof(int));
+  return kCounterBytes + (size_t)n_rows * n_heads * n_splits * kPartStride * sizeof(float);
 }
 
 }  // namespace wattn

@@ -24,8 +24,11 @@ constexpr int kHeadDim = 64;
 // there and the kernel winds down instead of hanging; wattn_device_status()
 // reads and clears it.
 
-// Wall-clock limit of one bounded wait, in nanoseconds (%globaltimer).
+// Limits of one bounded wait: wall clock (%globaltimer) and, independently,
+// the number of try_wait rounds (each suspends for at most kSuspendHintNs).
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
+constexpr uint32_t kSuspendHintNs = 1000;
+constexpr uint32_t kMaxWaitRounds = 4000000;  // >= 4 s of 1 us suspends
 
 WATTN_DEVINL unsigned long long globaltimer_ns() {
   unsigned long long t;
@@ -33,8 +36,10 @@ WATTN_DEVINL unsigned long long globaltimer_ns() {
   return t;
 }
 
-WATTN_DEVINL void report_timeout(int *status) {
-  atomicCAS(status, WATTN_OK, WATTN_ERR_TIMEOUT);
+// status[0]: status word; status[1]: site of the first wait that ran out
+// (kernel << 24 | role << 16 | barrier << 8 | iteration & 0xff).
+WATTN_DEVINL void report_timeout(int *status, int site) {
+  if (atomicCAS(status, WATTN_OK, WATTN_ERR_TIMEOUT) == WATTN_OK) atomicExch(status + 1, site);
 }
 
 // ------------------------------------------------------------ element types
@@ -119,10 +124,10 @@ WATTN_DEVINL bool mbar_try_wait(uint32_t bar_addr, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(bar_addr), "r"(parity)
+      : "r"(bar_addr), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return ok != 0;
 }
@@ -132,16 +137,16 @@ WATTN_DEVINL bool mbar_try_wait(uint32_t bar_addr, uint32_t parity) {
 // once; if the wait itself runs past kWaitLimitNs it reports a timeout,
 // sets *abort and returns false. Callers then wind down instead of hanging.
 WATTN_DEVINL bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort,
-                            int *status) {
+                            int *status, int site) {
   uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   unsigned long long t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(addr, parity)) return true;
-    if ((it & 63) == 0) {
+    if ((it & 15) == 0) {
       if (*abort) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
-        report_timeout(status);
+      if (globaltimer_ns() - t0 > kWaitLimitNs || it > kMaxWaitRounds) {
+        report_timeout(status, site);
         *abort = 1;
         return false;
       }
@@ -242,6 +247,20 @@ WATTN_DEVINL void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
         "=r"(r[31])
       : "r"(taddr));
+}
+
+// tcgen05.ld results are only valid after tcgen05.wait::ld, but the compiler
+// sees both as opaque asm and may move uses of the result registers above
+// the wait. Passing the registers through this empty volatile asm (ordered
+// after the wait like every volatile asm) pins all uses below it.
+WATTN_DEVINL void reg_fence(uint32_t (&r)[32]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]),
+                 "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+                 "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),
+                 "+r"(r[30]), "+r"(r[31]));
 }
 
 WATTN_DEVINL void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {

@@ -54,7 +54,9 @@ int launch_attn_f32(const float *q, const float *k, const float *v, float *o, in
 int launch_zero_rows(void *o, int out_dtype, int batch, int t, int width, int64_t o_rs,
                      int64_t o_bs, cudaStream_t stream);
 
-// Split-KV decode over dense K/V (decode.cu).
+// Split-KV decode over dense K/V (decode.cu). Counters of one launch are
+// indexed (row group, head) and must fit this fixed region.
+constexpr int kMaxSplitCounters = 65536;
 struct DecodePlan {
   int chunk;      // keys per split (multiple of 64)
   int n_splits;   // splits per (row chunk, head)

@@ -178,12 +178,12 @@ def multi_head_attention_with_cache(q, k, v, n_tokens, total_tokens, t_past, n_h
 
 
 def _dt_of(a) -> int:
-    name = str(a.dtype)
-    if name.endswith("float32"):
+    name = str(a.dtype).rsplit(".", 1)[-1]  # "torch.bfloat16" / numpy "float32"
+    if name == "float32":
         return F32
-    if name.endswith("float16"):
+    if name == "float16":
         return F16
-    if name.endswith("bfloat16"):
+    if name == "bfloat16":
         return BF16
     raise TypeError(f"unsupported dtype {a.dtype}")
 
