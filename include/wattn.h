@@ -125,6 +125,28 @@ int wattn_decode_fwd(const void *q, const void *k, const void *v, void *o,
                      float scale, void *workspace, size_t workspace_bytes,
                      void *stream);
 
+/* Decode without any allocation. This entry point has no counterpart in the
+ * reference: it exists for callers that may not allocate device memory at
+ * all (a real-time audio callback, a host whose allocator is frozen after
+ * start-up, a runtime that only hands out pre-registered buffers), so they
+ * can neither pass a workspace nor let wattn_decode_fwd allocate one.
+ * Same arguments and results as wattn_decode_fwd without the workspace: the
+ * split partials and merge counters live in an 8 MiB array compiled into
+ * the library, which every GPU that loads the library keeps until the
+ * process exits. A call whose plan needs more scratch than that returns
+ * WATTN_ERR_RANGE. The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress) with that device current; make that first
+ * call before any stream capture. All calls on a device share the array:
+ * calls whose kernels overlap on the GPU race and give wrong results. No
+ * cudaMalloc, cudaFree or other allocating routine is called. */
+int wattn_decode_fwd_noalloc(const void *q, const void *k, const void *v,
+                             void *o, int q_dtype, int kv_dtype,
+                             int out_dtype, int n_groups, int group_size,
+                             int t_kv, int n_heads, int d_head,
+                             int64_t q_row_stride, int64_t kv_row_stride,
+                             int64_t kv_group_stride, int64_t o_row_stride,
+                             float scale, void *stream);
+
 /* ======================================================================
  * Device-resident paged KV cache (replaces DecoderKvCache,
  * crates/whisper/src/decoder.rs:131-264, and the per-slot truncate/append

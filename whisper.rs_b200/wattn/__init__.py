@@ -27,7 +27,7 @@ __all__ = [
     "F32", "F16", "BF16", "WattnError", "lib", "LIB_PATH", "status_string",
     "flash_attention_2", "multi_head_attention", "single_token_mha_d64",
     "multi_head_attention_with_cache", "attention_host", "decode_host",
-    "attention_fwd", "decode_fwd", "decode_workspace_bytes", "DeviceKvCache",
+    "attention_fwd", "decode_fwd", "decode_fwd_noalloc", "decode_workspace_bytes", "DeviceKvCache",
     "device_status", "selftest_bounded_wait", "EXPORTED_SYMBOLS",
 ]
 
@@ -62,6 +62,8 @@ _SIGS = {
     "wattn_decode_workspace_bytes": (_sz, [_i, _i, _i, _i]),
     "wattn_decode_fwd": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i,
                               _i64, _i64, _i64, _i64, _f, _vp, _sz, _vp]),
+    "wattn_decode_fwd_noalloc": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i,
+                                      _i64, _i64, _i64, _i64, _f, _vp]),
     "wattn_kv_create": (_i, [ctypes.POINTER(_vp), _i, _i, _i, _i, _i, _i, _i, _i]),
     "wattn_kv_destroy": (_i, [_vp]),
     "wattn_kv_clear": (_i, [_vp]),
@@ -265,6 +267,22 @@ def decode_fwd(q, k, v, o, *, n_groups, group_size, t_kv, n_heads, scale, q_row_
                                 n_groups, group_size, t_kv, n_heads, 64, q_row_stride or w, kv_rs,
                                 kv_gs, o_row_stride or w, scale, ws_ptr, ws_bytes,
                                 _stream_ptr(stream)), "decode_fwd")
+
+
+def decode_fwd_noalloc(q, k, v, o, *, n_groups, group_size, t_kv, n_heads, scale,
+                       q_row_stride=None, kv_row_stride=None, kv_group_stride=None,
+                       o_row_stride=None, stream=None) -> None:
+    """``wattn_decode_fwd_noalloc``: decode_fwd for callers that must not
+    allocate device memory; its scratch is a fixed 8 MiB array inside the
+    library, shared by every call on a device (calls that overlap on the GPU
+    race)."""
+    w = n_heads * 64
+    kv_rs = kv_row_stride or w
+    kv_gs = kv_group_stride if kv_group_stride is not None else t_kv * kv_rs
+    _check(lib.wattn_decode_fwd_noalloc(_dev(q), _dev(k), _dev(v), _dev(o), _dt_of(q), _dt_of(k),
+                                        _dt_of(o), n_groups, group_size, t_kv, n_heads, 64,
+                                        q_row_stride or w, kv_rs, kv_gs, o_row_stride or w, scale,
+                                        _stream_ptr(stream)), "decode_fwd_noalloc")
 
 
 def device_status(device: int = -1) -> int:
