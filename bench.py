@@ -169,24 +169,24 @@ def barrier(world: int):
     torch.cuda.synchronize()
 
 
-def max_over_ranks(x: float, world: int) -> float:
+def _reduce(x: float, world: int, op: str) -> float:
     if world == 1:
         return x
     import torch
     import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
     return float(t.item())
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    """Max over ranks (the job time is the slowest rank's)."""
+    return _reduce(x, world, "max")
 
 
 def sum_over_ranks(x: float, world: int) -> float:
-    if world == 1:
-        return x
-    import torch
-    import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.SUM)
-    return float(t.item())
+    return _reduce(x, world, "sum")
 
 
 # --------------------------------------------------------------------- encoder (C3)
