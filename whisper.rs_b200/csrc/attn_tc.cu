@@ -6,12 +6,14 @@
 //
 //   * one CTA owns two 128-row query tiles of one (utterance, head); each
 //     tile has its own softmax warpgroup, so while one warpgroup turns S into
-//     P the tensor cores work on the other tile (ping-pong);
+//     P the tensor cores work on the other tile;
 //   * a TMA warp streams 128-key K and V tiles through a 3-deep ring in
 //     shared memory (128-byte swizzle, the layout UMMA reads directly);
 //   * an MMA warp issues tcgen05.mma: S = Q K^T (M=128, N=128, K=64) into
 //     tensor memory, then O += P V (M=128, N=64, K=128) with P read back from
-//     tensor memory;
+//     tensor memory. S(t, j+1) is issued as soon as the softmax has taken
+//     S(t, j) into registers, so the next scores are computed while the
+//     softmax works on the current ones;
 //   * the softmax warpgroup owns one query row per thread: it reads its S
 //     row from TMEM, keeps the running max m and normaliser l in registers
 //     (exp2 domain), rescales O in TMEM only when the max grows by more than
@@ -41,6 +43,10 @@ constexpr int kMmaWarp = kTmaWarp + 1;   // warp 9
 constexpr int kThreads = (kMmaWarp + 1) * 32;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+// One pair of exponentials in every kFmaExp2Every is computed on the FMA
+// pipe (exp2_fma2) instead of the SFU; 0 keeps them all on the SFU (the
+// faster setting measured so far on B200).
+constexpr int kFmaExp2Every = 0;
 
 struct Smem {
   uint8_t q[kTiles][kTileBytes];
@@ -49,8 +55,10 @@ struct Smem {
   uint64_t q_full;
   uint64_t k_full[kStages], k_empty[kStages];
   uint64_t v_full[kStages], v_empty[kStages];
-  uint64_t s_full[kTiles];  // S(t, j) ready and PV(t, j-1) done; last phase: O final
-  uint64_t p_full[kTiles];  // P(t, j) in TMEM and O(t) rescaled
+  uint64_t s_full[kTiles];  // S(t, j) in TMEM (MMA commit)
+  uint64_t s_free[kTiles];  // S(t, j) read into registers: S(t, j+1) may overwrite it
+  uint64_t p_full[kTiles];  // P(t, j) in TMEM and O(t) rescaled (softmax arrivals)
+  uint64_t o_done[kTiles];  // PV(t, j) complete: P(t, j+1) may be written (MMA commit)
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -66,28 +74,25 @@ struct Params {
   float scale_log2;  // scale * log2(e)
   int causal, q_pos_offset;
   int *status;
-#ifdef WATTN_TC_DEBUG
-  float *dbg;  // debug builds only: S, P of key tile 0, raw O and l per row
-#endif
 };
 
+// Normalises 64 accumulated dims by inv and stores them (16-byte stores).
 template <typename OutT>
-WATTN_DEVINL void store_row(OutT *dst, const float *o, float inv) {
+WATTN_DEVINL void store_row(OutT *dst, const uint32_t (&o)[2][32], float inv) {
+  auto at = [&](int i) { return __uint_as_float(o[i >> 5][i & 31]) * inv; };
   if constexpr (sizeof(OutT) == 4) {
     float4 *d4 = reinterpret_cast<float4 *>(dst);
 #pragma unroll
-    for (int c = 0; c < 16; ++c)
-      d4[c] = make_float4(o[4 * c] * inv, o[4 * c + 1] * inv, o[4 * c + 2] * inv,
-                          o[4 * c + 3] * inv);
+    for (int c = 0; c < 16; ++c) d4[c] = make_float4(at(4 * c), at(4 * c + 1), at(4 * c + 2), at(4 * c + 3));
   } else {
     uint4 *d4 = reinterpret_cast<uint4 *>(dst);
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
       uint4 w;
-      w.x = pack2<OutT>(o[8 * c + 0] * inv, o[8 * c + 1] * inv);
-      w.y = pack2<OutT>(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
-      w.z = pack2<OutT>(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
-      w.w = pack2<OutT>(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
+      w.x = pack2<OutT>(at(8 * c + 0), at(8 * c + 1));
+      w.y = pack2<OutT>(at(8 * c + 2), at(8 * c + 3));
+      w.z = pack2<OutT>(at(8 * c + 4), at(8 * c + 5));
+      w.w = pack2<OutT>(at(8 * c + 6), at(8 * c + 7));
       d4[c] = w;
     }
   }
@@ -121,7 +126,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int t = 0; t < kTiles; ++t) {
       mbar_init(&s.s_full[t], 1);
+      mbar_init(&s.s_free[t], kBM);
       mbar_init(&s.p_full[t], kBM);
+      mbar_init(&s.o_done[t], 1);
     }
     mbar_init(&s.drain, 1);
     s.abort = 0;
@@ -207,11 +214,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         umma_commit(&s.k_empty[0]);
       }
+      // Per key tile j: first S(t, j+1) for both tiles, as soon as the
+      // softmax has taken S(t, j) into registers (s_free), so the next
+      // scores are computed while the softmax works on this tile; then
+      // PV(t, j) once P(t, j) is in TMEM (p_full).
       for (int j = 0; ok && j < nkv; ++j) {
         const int st = j % kStages;
         const uint32_t ph = (j / kStages) & 1;
         const int jn = j + 1, stn = jn % kStages;
         const uint32_t phn = (jn / kStages) & 1;
+        if (jn < nkv) {
+          if (!mbar_wait(&s.k_full[stn], phn, abort, p.status, TC_SITE(2, 5, jn))) break;
+          for (int t = 0; t < n_tiles; ++t) {
+            if (!mbar_wait(&s.s_free[t], j & 1, abort, p.status, TC_SITE(2, 7 + t, j))) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(t, stn);
+            umma_commit(&s.s_full[t]);
+          }
+          if (!ok) break;
+          umma_commit(&s.k_empty[stn]);
+        }
         if (!mbar_wait(&s.v_full[st], ph, abort, p.status, TC_SITE(2, 2, j))) break;
         for (int t = 0; t < n_tiles; ++t) {
           if (!mbar_wait(&s.p_full[t], j & 1, abort, p.status, TC_SITE(2, 3 + t, j))) {
@@ -220,18 +245,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           issue_pv(t, st, j > 0);
-          if (t == n_tiles - 1) umma_commit(&s.v_empty[st]);
-          if (jn < nkv) {
-            if (t == 0 && !mbar_wait(&s.k_full[stn], phn, abort, p.status, TC_SITE(2, 5, jn))) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            issue_s(t, stn);
-            if (t == n_tiles - 1) umma_commit(&s.k_empty[stn]);
-          }
-          umma_commit(&s.s_full[t]);
+          umma_commit(&s.o_done[t]);
         }
+        if (!ok) break;
+        umma_commit(&s.v_empty[st]);
       }
       // Drain: every MMA issued above completes before TMEM is freed. This
       // wait ignores `abort` (it must outlive a wind-down) but stays bounded.
@@ -268,77 +285,110 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld();
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) reg_fence(r[q4]);
+        // S(t, j) is in registers: the MMA warp may compute S(t, j+1) now.
+        tc_fence_before();
+        mbar_arrive(&s.s_free[t]);
         float sv[128];
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4)
 #pragma unroll
           for (int i = 0; i < 32; ++i) sv[q4 * 32 + i] = __uint_as_float(r[q4][i]);
-#ifdef WATTN_TC_DEBUG
-        if (p.dbg && j == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
-          for (int i = 0; i < 128; ++i) p.dbg[(t * 128 + row) * 128 + i] = sv[i];
-#endif
         const int lim = key_lim - j * kBN;
         if (lim < kBN) {
 #pragma unroll
           for (int i = 0; i < 128; ++i)
             if (i >= lim) sv[i] = -INFINITY;
         }
-        float mx = sv[0];
+        // Row max: four independent chains of three-input max.
+        float mx4[4];
 #pragma unroll
-        for (int i = 1; i < 128; ++i) mx = fmaxf(mx, sv[i]);
+        for (int a = 0; a < 4; ++a) mx4[a] = fmax3(sv[a * 32], sv[a * 32 + 1], sv[a * 32 + 2]);
+#pragma unroll
+        for (int i = 3; i < 31; i += 2)
+#pragma unroll
+          for (int a = 0; a < 4; ++a) mx4[a] = fmax3(mx4[a], sv[a * 32 + i], sv[a * 32 + i + 1]);
+#pragma unroll
+        for (int a = 0; a < 4; ++a) mx4[a] = fmaxf(mx4[a], sv[a * 32 + 31]);
+        const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
         const float mc = mx * c;
-        // Lazy rescale. The TMEM accesses below are .sync.aligned, so the
-        // branch is taken by the whole warp whenever any lane needs it;
-        // lanes that do not need it rescale by 1.
+        // Lazy rescale: m only moves when the row max grows by more than
+        // 2^8, so p <= 256 and l, O stay exact; O itself is rescaled below,
+        // after the scores are dead (fewer live registers).
         const bool need = mc > m + kRescaleThreshold;
-        if (__any_sync(0xffffffffu, need)) {
-          const float alpha = need ? ex2(m - mc) : 1.f;  // 0 on the first tile (m = -inf)
+        const bool warp_need = __any_sync(0xffffffffu, need);
+        const float alpha = need ? ex2(m - mc) : 1.f;  // 0 on the first tile (m = -inf)
+        if (need) {
           l *= alpha;
-          if (j > 0) {
-            uint32_t o[2][32];
-            tmem_ld32(t_o, o[0]);
-            tmem_ld32(t_o + 32, o[1]);
-            tmem_wait_ld();
-            reg_fence(o[0]);
-            reg_fence(o[1]);
-#pragma unroll
-            for (int h2 = 0; h2 < 2; ++h2)
-#pragma unroll
-              for (int i = 0; i < 32; ++i)
-                o[h2][i] = __float_as_uint(__uint_as_float(o[h2][i]) * alpha);
-            tmem_st32(t_o, o[0]);
-            tmem_st32(t_o + 32, o[1]);
-          }
-          if (need) m = mc;
+          m = mc;
         }
         const float mu = (m == -INFINITY) ? 0.f : m;
-        uint32_t pk[2][32];
-        float lsum = 0.f;
+        const float2 c2 = make_float2(c, c), nmu2 = make_float2(-mu, -mu);
+        // P = 2^(s*c - mu), packed to 16-bit pairs (kept in registers until
+        // PV(t, j-1) is done, then stored to TMEM). l sums the *rounded*
+        // weights the tensor core multiplies V with: they then sum to
+        // exactly one and the rounding error of a dominant weight cancels
+        // in acc / l.
+        float2 acc2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                          make_float2(0.f, 0.f)};
+        uint32_t pk[64];
 #pragma unroll
         for (int i = 0; i < 64; ++i) {
-          const float p0 = ex2(fmaf(sv[2 * i], c, -mu));
-          const float p1 = ex2(fmaf(sv[2 * i + 1], c, -mu));
-          const uint32_t w = pack2<InT>(p0, p1);
-          pk[i >> 5][i & 31] = w;
-          // Normalise by the sum of the rounded weights the tensor core
-          // multiplies V with: the weights then sum to exactly one and the
-          // rounding error of a dominant weight cancels in acc / l.
-          const float2 r2 = unpack2<InT>(w);
-          lsum += r2.x + r2.y;
+          const float2 x = __ffma2_rn(make_float2(sv[2 * i], sv[2 * i + 1]), c2, nmu2);
+          float2 pv;
+          if (kFmaExp2Every > 0 && i % kFmaExp2Every == kFmaExp2Every - 1) {
+            pv = exp2_fma2(x);
+          } else {
+            pv.x = ex2(x.x);
+            pv.y = ex2(x.y);
+          }
+          const uint32_t w = pack2<InT>(pv.x, pv.y);
+          pk[i] = w;
+          acc2[i & 3] = __fadd2_rn(acc2[i & 3], unpack2<InT>(w));
         }
-        l += lsum;
-#ifdef WATTN_TC_DEBUG
-        if (p.dbg && j == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
-          for (int i = 0; i < 128; ++i)
-            p.dbg[32768 + (t * 128 + row) * 128 + i] = ex2(fmaf(sv[i], c, -mu));
-#endif
-        tmem_st32(t_p, pk[0]);
-        tmem_st32(t_p + 32, pk[1]);
+        l += (acc2[0].x + acc2[0].y) + (acc2[1].x + acc2[1].y) + (acc2[2].x + acc2[2].y) +
+             (acc2[3].x + acc2[3].y);
+        // P(t, j) may only overwrite P(t, j-1) once PV(t, j-1) has read it,
+        // and O may only be rescaled once PV(t, j-1) has added to it.
+        if (j > 0) {
+          const bool done =
+              mbar_wait(&s.o_done[t], (j - 1) & 1, abort, p.status, TC_SITE(3 + t, 2, j));
+          if (!__all_sync(0xffffffffu, done)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+        // O rescale for the rows whose max moved. The TMEM accesses are
+        // .sync.aligned, so the whole warp takes the branch when any lane
+        // needs it; other lanes scale by 1.
+        if (warp_need && j > 0) {
+          uint32_t o[2][32];
+          tmem_ld32(t_o, o[0]);
+          tmem_ld32(t_o + 32, o[1]);
+          tmem_wait_ld();
+          reg_fence(o[0]);
+          reg_fence(o[1]);
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2)
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              o[h2][i] = __float_as_uint(__uint_as_float(o[h2][i]) * alpha);
+          tmem_st32(t_o, o[0]);
+          tmem_st32(t_o + 32, o[1]);
+        }
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint32_t chunk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) chunk[i] = pk[q4 * 16 + i];
+          tmem_st16(t_p + q4 * 16, chunk);
+        }
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&s.p_full[t]);
       }
-      const bool fin = ok && mbar_wait(&s.s_full[t], nkv & 1, abort, p.status, TC_SITE(3 + t, 1, nkv));
+      const bool fin =
+          ok && mbar_wait(&s.o_done[t], (nkv - 1) & 1, abort, p.status, TC_SITE(3 + t, 1, nkv));
       if (__all_sync(0xffffffffu, fin)) {
         tc_fence_after();
         uint32_t o[2][32];
@@ -347,26 +397,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld();
         reg_fence(o[0]);
         reg_fence(o[1]);
-#ifdef WATTN_TC_DEBUG
-        if (p.dbg && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) {
-          for (int i = 0; i < 32; ++i) {
-            p.dbg[65536 + (t * 128 + row) * 64 + i] = __uint_as_float(o[0][i]);
-            p.dbg[65536 + (t * 128 + row) * 64 + 32 + i] = __uint_as_float(o[1][i]);
-          }
-          p.dbg[65536 + 16384 + t * 128 + row] = l;
-        }
-#endif
         if (qrow < p.t_q) {
-          float of[64];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            of[i] = __uint_as_float(o[0][i]);
-            of[32 + i] = __uint_as_float(o[1][i]);
-          }
           const float inv = l > 0.f ? 1.f / l : 0.f;
           OutT *dst = reinterpret_cast<OutT *>(p.o) + (int64_t)b * p.o_bs +
                       (int64_t)qrow * p.o_rs + head * kHeadDim;
-          store_row<OutT>(dst, of, inv);
+          store_row<OutT>(dst, o, inv);
         }
       }
     }
@@ -409,11 +444,6 @@ int make_qkv_map(CUtensorMap *map, const void *base, int dt, int n_heads, int t,
 
 }  // namespace
 
-#ifdef WATTN_TC_DEBUG
-float *g_tc_dbg = nullptr;
-extern "C" void wattn_debug_set_tc_dump(float *p) { g_tc_dbg = p; }
-#endif
-
 int launch_attn_tc(const void *q, const void *k, const void *v, void *o, int in_dtype,
                    int out_dtype, int batch, int t_q, int t_kv, int n_heads, int64_t q_rs,
                    int64_t kv_rs, int64_t o_rs, int64_t q_bs, int64_t kv_bs, int64_t o_bs,
@@ -434,9 +464,6 @@ int launch_attn_tc(const void *q, const void *k, const void *v, void *o, int in_
   p.q_pos_offset = q_pos_offset;
   p.status = device_status_ptr();
   if (p.status == nullptr) return WATTN_ERR_CUDA;
-#ifdef WATTN_TC_DEBUG
-  p.dbg = g_tc_dbg;
-#endif
   if (in_dtype == WATTN_F16) {
     if (out_dtype == WATTN_F32)
       return launch_typed<WATTN_F16, WATTN_F32>(mq, mk, mv, p, batch, n_heads, stream);

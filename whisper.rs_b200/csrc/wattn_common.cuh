@@ -90,6 +90,35 @@ WATTN_DEVINL float ex2(float x) {
   return y;
 }
 
+// max(a, b, c) in one instruction (sm_100 three-input max).
+WATTN_DEVINL float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x for a pair on the FMA pipe, for x <= 8 (x below -126 gives ~0).
+// Range reduction x = j + f with j = rint(x) (the 1.5 * 2^23 rounding trick)
+// and f in [-1/2, 1/2]; 2^f from a cubic fitted for minimum relative error on
+// that interval (a discretised Chebyshev fit solved as a linear programme,
+// exp2_poly.py: max relative error 7.5e-5 after f32 evaluation, below the
+// bf16 / f16 rounding of P); 2^j is applied by adding j to the exponent.
+WATTN_DEVINL float2 exp2_fma2(float2 x) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  x.x = fmaxf(x.x, -126.0f);
+  x.y = fmaxf(x.y, -126.0f);
+  const float2 t = __fadd2_rn(x, make_float2(kMagic, kMagic));
+  const float2 j = __fadd2_rn(t, make_float2(-kMagic, -kMagic));
+  const float2 f = __ffma2_rn(j, make_float2(-1.0f, -1.0f), x);
+  float2 p = __ffma2_rn(make_float2(5.517221987e-02f, 5.517221987e-02f), f,
+                        make_float2(2.426111549e-01f, 2.426111549e-01f));
+  p = __ffma2_rn(p, f, make_float2(6.932608485e-01f, 6.932608485e-01f));
+  p = __ffma2_rn(p, f, make_float2(9.999280572e-01f, 9.999280572e-01f));
+  // The low mantissa bits of t hold j + 2^22; shifting by 23 drops the rest.
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
+}
+
 // ------------------------------------------------------------ shared memory
 WATTN_DEVINL uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -247,6 +276,17 @@ WATTN_DEVINL void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
         "=r"(r[31])
       : "r"(taddr));
+}
+
+// 16 consecutive 32-bit columns of this thread's TMEM lane.
+WATTN_DEVINL void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
 }
 
 // tcgen05.ld results are only valid after tcgen05.wait::ld, but the compiler
