@@ -329,6 +329,8 @@ int validate_decode(const void *q, const void *k, const void *v, const void *o, 
     return set_error(WATTN_ERR_INVALID,
                      "k/v must be 16-byte aligned with row and group strides that are multiples "
                      "of 16 bytes");
+  if (q_dt != WATTN_F32 && ((reinterpret_cast<uintptr_t>(q) & 3) || (q_rs & 1)))
+    return set_error(WATTN_ERR_INVALID, "16-bit q must be 4-byte aligned with an even row stride");
   return WATTN_OK;
 }
 

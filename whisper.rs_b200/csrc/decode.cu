@@ -27,6 +27,8 @@
 #include "wattn_common.cuh"
 #include "wattn_internal.h"
 
+#include <type_traits>
+
 namespace wattn {
 
 constexpr int kDecSub = 64;        // keys per sub-tile (TMA box rows)
@@ -75,6 +77,52 @@ struct DecSmem {
   int abort;
   int last;
 };
+
+// Shared memory of the tensor-core path: no score or query buffers (the
+// scores stay in mma fragments), so three CTAs fit on an SM.
+template <int KV_DT>
+struct DecSmemMma {
+  static constexpr int S = KvGeom<KV_DT>::max_subs;
+  uint8_t k[S][KvGeom<KV_DT>::sub_bytes];
+  uint8_t v[S][KvGeom<KV_DT>::sub_bytes];
+  float m[kDecRows], l[kDecRows];
+  float wm[4][kDecRows], wl[4][kDecRows];  // per-warp max / normaliser
+  uint64_t kbar[S], vbar[S];
+  int abort;
+  int last;
+};
+
+// Warp-level tensor-core helpers (mma.sync m16n8k16, f32 accumulation).
+template <typename T>
+WATTN_DEVINL void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if constexpr (sizeof(T) == 2 && __is_same(T, __nv_bfloat16)) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+
+// Four 8x8 16-bit matrices from shared memory; lane i addresses row i % 8 of
+// matrix i / 8. The .trans form delivers them transposed.
+WATTN_DEVINL void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+WATTN_DEVINL void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2,
+                            uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
 
 // Byte offset of 16-byte chunk `c` of row `r` in a 128-byte-swizzled tile.
 WATTN_DEVINL int swz(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
@@ -150,14 +198,20 @@ WATTN_DEVINL void store_out(void *o, int64_t off, float x) {
 }
 
 // Shared body. PAGED selects how a sub-tile's TMA coordinates are formed.
+// Tensor-core path: 16-bit K/V with a query of the same type.
+template <int Q_DT, int KV_DT>
+constexpr bool kDecUseMma = KV_DT != WATTN_F32 && Q_DT == KV_DT;
+
 template <int Q_DT, int KV_DT, int OUT_DT, bool PAGED>
 __device__ void decode_body(const CUtensorMap &map_k, const CUtensorMap &map_v,
                             const DecParams &p, const PagedTable *pt) {
   using QT = typename Elem<Q_DT>::T;
   using OutT = typename Elem<OUT_DT>::T;
   using G = KvGeom<KV_DT>;
+  constexpr bool kMma = kDecUseMma<Q_DT, KV_DT>;
+  using SmemT = typename std::conditional<kMma, DecSmemMma<KV_DT>, DecSmem<KV_DT>>::type;
   extern __shared__ uint8_t dec_smem_raw[];
-  DecSmem<KV_DT> &s = *reinterpret_cast<DecSmem<KV_DT> *>(
+  SmemT &s = *reinterpret_cast<SmemT *>(
       (reinterpret_cast<uintptr_t>(dec_smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int split = blockIdx.x, head = blockIdx.y;
@@ -223,6 +277,125 @@ __device__ void decode_body(const CUtensorMap &map_k, const CUtensorMap &map_v,
     }
   }
 
+  // Per-warp partial outputs, summed over the warps below, in the (now idle)
+  // K buffer: [4 warps][kDecRows][64] floats.
+  float *red = reinterpret_cast<float *>(&s.k[0][0]);
+  if constexpr (kMma) {
+    // ---- tensor-core path. Warp w takes keys 16w..16w+15 of every 64-key
+    // sub-tile. S = Q K^T and O += P V with mma.sync m16n8k16 (rows = query
+    // rows of the group, padded to 16; the scale is applied in f32 to S),
+    // online softmax per row in the exp2 domain on the accumulator
+    // fragments, then the four warps merge by log-sum-exp.
+    const int g = lane >> 2, t4 = lane & 3;
+    volatile int *abort = &s.abort;
+    uint32_t qa[4][4];
+    {
+      const uint32_t *qrow = reinterpret_cast<const uint32_t *>(
+          reinterpret_cast<const QT *>(p.q) + (int64_t)(row0 + g) * p.q_rs + head * 64);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        qa[ks][0] = g < nr ? qrow[ks * 8 + t4] : 0u;
+        qa[ks][2] = g < nr ? qrow[ks * 8 + 4 + t4] : 0u;
+        qa[ks][1] = qa[ks][3] = 0u;  // rows 8..15 of the tile: beyond the 8 rows of a CTA
+      }
+    }
+    const float c = p.scale_log2;
+    float m_r = -INFINITY, l_r = 0.f;
+    float acc[8][4];
+#pragma unroll
+    for (int db = 0; db < 8; ++db) acc[db][0] = acc[db][1] = acc[db][2] = acc[db][3] = 0.f;
+    __syncthreads();  // barrier initialisation visible to every warp
+    const int kb = warp * 16;
+    for (int st = 0; st < n_sub; ++st) {
+      mbar_wait(&s.kbar[st], 0, abort, p.status, (2 << 24) | (1 << 16) | (st << 8));
+      const uint32_t ktile = smem_u32(s.k[st]), vtile = smem_u32(s.v[st]);
+      float sc[2][4];
+#pragma unroll
+      for (int nb = 0; nb < 2; ++nb) {
+        sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.f;
+        const int key_row = kb + nb * 8 + (lane & 7);
+#pragma unroll
+        for (int ks2 = 0; ks2 < 2; ++ks2) {
+          uint32_t r0, r1, r2, r3;
+          const int chunk = 4 * ks2 + (lane >> 3);
+          ldsm_x4(ktile + key_row * 128 + ((chunk ^ (key_row & 7)) << 4), r0, r1, r2, r3);
+          mma16816<QT>(sc[nb], qa[2 * ks2], r0, r1);
+          mma16816<QT>(sc[nb], qa[2 * ks2 + 1], r2, r3);
+        }
+      }
+      // Mask keys outside [kv_lo, kv_hi) (row g holds keys 2*t4, 2*t4+1 of each 8).
+      const int key0 = k_beg + st * kDecSub + kb + 2 * t4;
+#pragma unroll
+      for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int key = key0 + nb * 8 + e;
+          if (key < kv_lo || key >= kv_hi) sc[nb][e] = -INFINITY;
+        }
+      float mx = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float mc = mx * c;
+      if (mc > m_r + 8.0f) {  // lazy rescale, as in the encoder kernel
+        const float alpha = ex2(m_r - mc);
+        l_r *= alpha;
+#pragma unroll
+        for (int db = 0; db < 8; ++db) {
+          acc[db][0] *= alpha;
+          acc[db][1] *= alpha;
+        }
+        m_r = mc;
+      }
+      const float mu = (m_r == -INFINITY) ? 0.f : m_r;
+      float pe[2][2];
+#pragma unroll
+      for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) pe[nb][e] = ex2(fmaf(sc[nb][e], c, -mu));
+      uint32_t pa[4];
+      pa[0] = pack2<QT>(pe[0][0], pe[0][1]);
+      pa[2] = pack2<QT>(pe[1][0], pe[1][1]);
+      pa[1] = pa[3] = 0u;
+      // Normalise by the rounded weights the tensor core uses.
+      {
+        const float2 r0 = unpack2<QT>(pa[0]), r2 = unpack2<QT>(pa[2]);
+        l_r += (r0.x + r0.y) + (r2.x + r2.y);
+      }
+      mbar_wait(&s.vbar[st], 0, abort, p.status, (2 << 24) | (2 << 16) | (st << 8));
+      {
+        const int key_row = kb + ((lane >> 3) & 1) * 8 + (lane & 7);
+#pragma unroll
+        for (int db2 = 0; db2 < 4; ++db2) {
+          uint32_t r0, r1, r2, r3;
+          const int chunk = db2 * 2 + (lane >> 4);
+          ldsm_x4_t(vtile + key_row * 128 + ((chunk ^ (key_row & 7)) << 4), r0, r1, r2, r3);
+          mma16816<QT>(acc[2 * db2], pa, r0, r1);
+          mma16816<QT>(acc[2 * db2 + 1], pa, r2, r3);
+        }
+      }
+    }
+    l_r += __shfl_xor_sync(0xffffffffu, l_r, 1);
+    l_r += __shfl_xor_sync(0xffffffffu, l_r, 2);
+    // Merge the four warps (log-sum-exp) into red / s.m / s.l.
+    __syncthreads();  // every warp is done with K: `red` may overwrite it
+    if (t4 == 0 && g < kDecRows) s.wm[warp][g] = m_r;
+    __syncthreads();
+    if (g < nr) {
+      const float M = fmaxf(fmaxf(s.wm[0][g], s.wm[1][g]), fmaxf(s.wm[2][g], s.wm[3][g]));
+      const float w = (m_r == -INFINITY) ? 0.f : ex2(m_r - M);
+#pragma unroll
+      for (int db = 0; db < 8; ++db)
+        *reinterpret_cast<float2 *>(&red[(warp * kDecRows + g) * 64 + db * 8 + 2 * t4]) =
+            make_float2(acc[db][0] * w, acc[db][1] * w);
+      if (t4 == 0) {
+        s.wl[warp][g] = l_r * w;
+        if (warp == 0) s.m[g] = M;
+      }
+    }
+    __syncthreads();
+    if (tid < nr) s.l[tid] = s.wl[0][tid] + s.wl[1][tid] + s.wl[2][tid] + s.wl[3][tid];
+    __syncthreads();
+  } else {
   // Query rows, pre-scaled into the exp2 domain.
   for (int i = tid; i < kDecRows * 64; i += kDecThreads) {
     const int r = i >> 6, d = i & 63;
@@ -293,12 +466,13 @@ __device__ void decode_body(const CUtensorMap &map_k, const CUtensorMap &map_v,
     }
   }
   // Cross-warp sum through the (now idle) K buffer.
-  float *red = reinterpret_cast<float *>(&s.k[0][0]);  // [4 warps][kDecRows][64]
 #pragma unroll
   for (int r = 0; r < kDecRows; ++r)
     if (r < nr) *reinterpret_cast<float2 *>(&red[(warp * kDecRows + r) * 64 + 2 * lane]) =
         make_float2(acc[r][0], acc[r][1]);
   __syncthreads();
+
+  }
 
   const int64_t part_base = (int64_t)row0 * p.n_heads;  // row-major partial index base
   for (int i = tid; i < nr * 64; i += kDecThreads) {
@@ -361,8 +535,9 @@ __global__ void __launch_bounds__(kDecThreads)
   decode_body<Q_DT, KV_DT, OUT_DT, true>(map_k, map_v, p, &pt);
 }
 
-template <int KV_DT> constexpr int dec_smem_bytes() {
-  return (int)sizeof(DecSmem<KV_DT>) + 1024;
+template <int Q_DT, int KV_DT> constexpr int dec_smem_bytes() {
+  return (kDecUseMma<Q_DT, KV_DT> ? (int)sizeof(DecSmemMma<KV_DT>) : (int)sizeof(DecSmem<KV_DT>)) +
+         1024;
 }
 
 template <typename K>
@@ -377,7 +552,7 @@ template <int Q_DT, int KV_DT, int OUT_DT>
 int launch_dense_typed(const CUtensorMap &mk, const CUtensorMap &mv, const DecParams &p,
                        int n_groups, cudaStream_t stream) {
   auto kern = decode_dense_kernel<Q_DT, KV_DT, OUT_DT>;
-  const int smem = dec_smem_bytes<KV_DT>();
+  const int smem = dec_smem_bytes<Q_DT, KV_DT>();
   int rc = set_smem(kern, smem);
   if (rc != WATTN_OK) return rc;
   dim3 grid(p.n_splits, p.n_heads, n_groups * p.row_chunks);
@@ -389,7 +564,7 @@ template <int Q_DT, int KV_DT, int OUT_DT>
 int launch_paged_typed(const CUtensorMap &mk, const CUtensorMap &mv, const DecParams &p,
                        const PagedTable &pt, int max_splits, cudaStream_t stream) {
   auto kern = decode_paged_kernel<Q_DT, KV_DT, OUT_DT>;
-  const int smem = dec_smem_bytes<KV_DT>();
+  const int smem = dec_smem_bytes<Q_DT, KV_DT>();
   int rc = set_smem(kern, smem);
   if (rc != WATTN_OK) return rc;
   dim3 grid(max_splits, p.n_heads, pt.n_rows);

@@ -488,6 +488,8 @@ int wattn_kv_attend(wattn_kv_cache *c, int layer, const int *slots, const int *n
   }
   if (total == 0) return WATTN_OK;
   if (!q || !o) return set_error(WATTN_ERR_INVALID, "kv_attend: NULL q/o");
+  if (q_dtype != WATTN_F32 && ((reinterpret_cast<uintptr_t>(q) & 3) || (q_row_stride & 1)))
+    return set_error(WATTN_ERR_INVALID, "kv_attend: 16-bit q must be 4-byte aligned with an even row stride");
 
   // Default workspace: owned by the cache, zeroed once, grown on demand.
   const size_t need = wattn_kv_workspace_bytes(c, total);
