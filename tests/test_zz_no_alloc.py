@@ -61,14 +61,19 @@ def test_noalloc_decode_matches_workspace_decode_twice(W):
 
 def test_noalloc_rejects_calls_beyond_its_scratch(W):
     import torch
-    n_groups, g, t_kv, h = 400, 5, 1500, 20   # partials far beyond the fixed 8 MiB
+    # f32 K/V take the CUDA-core kernel, whose 12 splits of 128 keys here need
+    # 800 rows x 20 heads x 12 partials (~51 MB), far beyond the fixed 8 MiB.
+    # K/V are allocated at full size so that nothing is read out of bounds
+    # even if the call were accepted.
+    n_groups, g, t_kv, h = 100, 8, 1500, 20
     d = h * 64
-    q = torch.zeros(n_groups * g * d, dtype=torch.half, device="cuda")
-    kv = torch.zeros(16 * d, dtype=torch.half, device="cuda")  # never read: rejected first
+    q = torch.zeros(n_groups * g * d, device="cuda")
+    kv = torch.zeros(n_groups * t_kv * d, device="cuda")
     out = torch.zeros(n_groups * g * d, device="cuda")
     rc = W.lib.wattn_decode_fwd_noalloc(q.data_ptr(), kv.data_ptr(), kv.data_ptr(), out.data_ptr(),
-                                        W.F16, W.F16, W.F32, n_groups, g, t_kv, h, 64, d, d, 0, d,
-                                        0.125, None)
+                                        W.F32, W.F32, W.F32, n_groups, g, t_kv, h, 64, d, d,
+                                        t_kv * d, d, 0.125, None)
+    torch.cuda.synchronize()
     assert rc == -6
     buf = ctypes.create_string_buffer(256)
     W.lib.wattn_last_error(buf, 256)

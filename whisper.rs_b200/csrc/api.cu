@@ -342,7 +342,7 @@ int decode_device(const void *q, const void *k, const void *v, void *o, int q_dt
   if (t_kv == 0)
     return launch_zero_rows(o, out_dt, 1, n_groups * group_size, n_heads * kHeadDim, o_rs, 0, st);
   if (ws == nullptr) {
-    const DecodePlan pl = plan_decode(n_groups, group_size, t_kv, n_heads, kv_dt);
+    const DecodePlan pl = plan_decode(n_groups, group_size, t_kv, n_heads, q_dt, kv_dt);
     ws = thread_workspace(pl.workspace_bytes, st);
     if (ws == nullptr) return set_error(WATTN_ERR_NOMEM, "decode workspace allocation failed");
     ws_bytes = std::max(pl.workspace_bytes, (size_t)1 << 20);
@@ -420,7 +420,7 @@ int decode_host(const void *q, const void *k, const void *v, void *o, int q_dt, 
   const size_t per = round_up(qb, 256) + 2 * kvb_dev + round_up(ob, 256);
   const int chunk = (int)std::max<size_t>(1, std::min<size_t>(n_groups, ((size_t)64 << 20) / per));
   int rc = WATTN_OK;
-  const DecodePlan pl = plan_decode(chunk, group_size, t_kv, n_heads, kv_dt);
+  const DecodePlan pl = plan_decode(chunk, group_size, t_kv, n_heads, q_dt, kv_dt);
   for (int i = 0; i < 2 && rc == WATTN_OK; ++i) {
     rc = grow(&h->buf[i], &h->buf_bytes[i], per * chunk, false, h->st[i]);
     if (rc == WATTN_OK) rc = grow(&h->ws[i], &h->ws_bytes[i], pl.workspace_bytes, true, h->st[i]);
@@ -529,10 +529,13 @@ int wattn_attention_fwd(const void *q, const void *k, const void *v, void *o, in
 
 size_t wattn_decode_workspace_bytes(int n_groups, int group_size, int t_kv, int n_heads) {
   if (n_groups <= 0 || group_size <= 0 || t_kv <= 0 || n_heads <= 0) return 0;
-  // The f16/bf16 plan has the most splits; it bounds the f32 plan too.
-  const DecodePlan a = plan_decode(n_groups, group_size, t_kv, n_heads, WATTN_F16);
-  const DecodePlan b = plan_decode(n_groups, group_size, t_kv, n_heads, WATTN_F32);
-  return std::max(a.workspace_bytes, b.workspace_bytes);
+  // The largest of the plans of the three kernel families (tensor-core,
+  // CUDA-core over 16-bit K/V, CUDA-core over f32 K/V), so the size serves
+  // every dtype combination.
+  const DecodePlan a = plan_decode(n_groups, group_size, t_kv, n_heads, WATTN_F16, WATTN_F16);
+  const DecodePlan b = plan_decode(n_groups, group_size, t_kv, n_heads, WATTN_F32, WATTN_F16);
+  const DecodePlan c = plan_decode(n_groups, group_size, t_kv, n_heads, WATTN_F32, WATTN_F32);
+  return std::max(a.workspace_bytes, std::max(b.workspace_bytes, c.workspace_bytes));
 }
 
 int wattn_decode_fwd(const void *q, const void *k, const void *v, void *o, int q_dtype,

@@ -5,37 +5,49 @@
 // over the 1500 encoder states) and, over the paged cache, the causal
 // self-attention of multi_head_attention_with_cache (decoder.rs:835-892).
 //
-// Structure (one CTA = 4 warps per (split of the keys, head, group of <= 8
-// query rows)):
-//   * thread 0 issues every TMA load of the split up front: 64-key K and V
-//     sub-tiles, 128-byte swizzled, one mbarrier each, so all of a CTA's
-//     bytes are in flight at once and two or three CTAs per SM keep HBM busy;
-//   * scores: two lanes per key (32 dims each) against every query row of the
-//     group, q pre-scaled by scale*log2(e) and broadcast from shared memory.
-//     The query rows of one group share each K/V byte loaded (the beams of an
-//     utterance share its cross-attention K/V), so the bytes per row fall
-//     with the group size;
-//   * exact softmax over the split (max, exp2, sum), then P V with each lane
-//     owning two output dims;
-//   * splits are merged by a log-sum-exp reduction done by the last CTA of
-//     each (row group, head) to finish (a device counter in the workspace,
-//     reset by that CTA), so there is no second kernel launch.
+// One CTA serves (a split of the keys, a head, a group of <= 8 query rows).
+// The query rows of one group share every K/V byte loaded (the beams of an
+// utterance share its cross-attention K/V), so the bytes per row fall with
+// the group size. K/V arrive as 64-key sub-tiles by TMA, 128-byte swizzled.
+//
+// Tensor-core path (16-bit K/V and a query of the same type), a streaming
+// kernel: a producer warp keeps a ring of kStrStages sub-tiles full while
+// four compute warps consume it, so each CTA has up to four sub-tiles (64 KB)
+// in flight for its whole life. Splits are few and long (about three waves of
+// CTAs over the GPU): S = Q K^T and O += P V run on mma.sync m16n8k16 with an
+// online softmax on the accumulator fragments; the four warps merge by
+// log-sum-exp.
+//
+// CUDA-core path (f32 K/V, or a query type other than the K/V type): thread 0
+// issues every load of a short split up front; two lanes per key form the
+// scores, an exact softmax over the split follows, then P V with each lane
+// owning two output dims.
+//
+// Either way, splits of one (row group, head) are merged by a log-sum-exp
+// reduction in the last CTA to finish (a device counter in the workspace,
+// reset by that CTA), so there is no second kernel launch.
 // The reference skips values whose probability is below 1e-7
-// (attention.rs:366,425); this kernel does not (the skip changes a result by
+// (attention.rs:366,425); these kernels do not (the skip changes a result by
 // at most t_kv * 1e-7 * max|v|).
 
 #include "wattn_common.cuh"
 #include "wattn_internal.h"
 
-#include <type_traits>
+#include <algorithm>
 
 namespace wattn {
 
 constexpr int kDecSub = 64;        // keys per sub-tile (TMA box rows)
 constexpr int kDecRows = 8;        // query rows per CTA
-constexpr int kDecThreads = 128;
-constexpr int kDecMaxSubs = 4;     // sub-tiles per split (chunk <= 256 keys; 128 for f32)
+constexpr int kDecThreads = 128;   // CUDA-core path
+constexpr int kDecMaxSubs = 4;     // CUDA-core path: sub-tiles per split (chunk <= 256 keys; 128 for f32)
 constexpr int kPartStride = 66;    // floats per partial: acc[64], m, l
+constexpr int kStrStages = 4;      // tensor-core path: depth of the K/V ring (sub-tiles)
+constexpr int kStrWarps = 4;       // compute warps; one more warp issues the loads
+constexpr int kStrThreads = (kStrWarps + 1) * 32;
+constexpr int kStrSlots = 148 * 3; // resident tensor-core CTAs on a B200: three per SM
+constexpr int kStrMinSubs = 4;     // sub-tiles per split below which no further split is made
+constexpr bool kStrPagedPersist = false;  // paged rows vary in length: one item per CTA
 // Workspace layout, the same for every call: [counters][partials]. The
 // counter region has a fixed size, so partials written by one call can never
 // land where a later call of another shape keeps its counters; every call
@@ -59,12 +71,14 @@ struct DecParams {
   int64_t q_rs, o_rs;
   int group_size, t_kv, n_heads;
   int row_chunks, n_splits, chunk;
+  int n_items;   // tensor-core path: (split, head, row chunk) items, walked by a persistent grid
   float scale_log2;
   float *part;   // [rows][n_heads][n_splits][kPartStride]
   int *count;    // [row groups][n_heads]
   int *status;
 };
 
+// Shared memory of the CUDA-core path: every sub-tile of the split at once.
 template <int KV_DT>
 struct DecSmem {
   static constexpr int S = KvGeom<KV_DT>::max_subs;
@@ -78,16 +92,18 @@ struct DecSmem {
   int last;
 };
 
-// Shared memory of the tensor-core path: no score or query buffers (the
-// scores stay in mma fragments), so three CTAs fit on an SM.
+// Shared memory of the tensor-core path: the K/V ring (64 KB for 16-bit
+// K/V, so three CTAs share an SM) and the cross-warp merge buffers (the
+// ring keeps streaming the next item during a merge). The scores stay in
+// mma fragments.
 template <int KV_DT>
-struct DecSmemMma {
-  static constexpr int S = KvGeom<KV_DT>::max_subs;
-  uint8_t k[S][KvGeom<KV_DT>::sub_bytes];
-  uint8_t v[S][KvGeom<KV_DT>::sub_bytes];
+struct StreamSmem {
+  uint8_t k[kStrStages][KvGeom<KV_DT>::sub_bytes];
+  uint8_t v[kStrStages][KvGeom<KV_DT>::sub_bytes];
+  float red[kStrWarps][kDecRows][64];  // per-warp partial outputs of an item
   float m[kDecRows], l[kDecRows];
-  float wm[4][kDecRows], wl[4][kDecRows];  // per-warp max / normaliser
-  uint64_t kbar[S], vbar[S];
+  float wm[kStrWarps][kDecRows], wl[kStrWarps][kDecRows];  // per-warp max / normaliser
+  uint64_t kfull[kStrStages], vfull[kStrStages], empty[kStrStages];
   int abort;
   int last;
 };
@@ -197,118 +213,241 @@ WATTN_DEVINL void store_out(void *o, int64_t off, float x) {
   reinterpret_cast<OutT *>(o)[off] = from_f32<OutT>(x);
 }
 
-// Shared body. PAGED selects how a sub-tile's TMA coordinates are formed.
-// Tensor-core path: 16-bit K/V with a query of the same type.
-template <int Q_DT, int KV_DT>
-constexpr bool kDecUseMma = KV_DT != WATTN_F32 && Q_DT == KV_DT;
+// Query rows of one work item and the physical key range [kv_lo, kv_hi)
+// they attend; `cnt_idx` is the item's split counter.
+struct DecRows {
+  int row0, nr, kv_lo, kv_hi, group, cnt_idx;
+};
 
-template <int Q_DT, int KV_DT, int OUT_DT, bool PAGED>
-__device__ void decode_body(const CUtensorMap &map_k, const CUtensorMap &map_v,
-                            const DecParams &p, const PagedTable *pt) {
-  using QT = typename Elem<Q_DT>::T;
-  using OutT = typename Elem<OUT_DT>::T;
+// One work item: split `split` of the keys of (row chunk / paged row z,
+// head). `k_beg` is its first key and `n_sub` its sub-tiles; an item past
+// the end of its row's keys (paged rows shorter than the longest) is empty.
+struct DecWork {
+  DecRows rw;
+  int head, split, n_splits, k_beg, n_sub;
+};
+
+template <bool PAGED>
+WATTN_DEVINL DecWork dec_work(const DecParams &p, const PagedTable *pt, int split, int head,
+                              int z) {
+  DecWork w;
+  DecRows &r = w.rw;
+  if constexpr (PAGED) {
+    r.row0 = z;
+    r.nr = 1;
+    r.kv_lo = pt->kv_lo[z];
+    r.kv_hi = pt->kv_hi[z];
+    r.group = 0;
+  } else {
+    r.group = z / p.row_chunks;
+    const int rc = z % p.row_chunks;
+    r.row0 = r.group * p.group_size + rc * kDecRows;
+    r.nr = min(kDecRows, p.group_size - rc * kDecRows);
+    r.kv_lo = 0;
+    r.kv_hi = p.t_kv;
+  }
+  r.cnt_idx = z * p.n_heads + head;
+  w.head = head;
+  w.split = split;
+  const int base = r.kv_lo & ~(kDecSub - 1);  // sub-tiles start on 64-row marks
+  w.n_splits = (r.kv_hi - base + p.chunk - 1) / p.chunk;
+  w.k_beg = base + split * p.chunk;
+  w.n_sub = w.k_beg < r.kv_hi ? min(p.chunk, r.kv_hi - w.k_beg + kDecSub - 1) / kDecSub : 0;
+  return w;
+}
+
+// Item `it` of the tensor-core grid: split fastest, then head, then row
+// chunk, so the items running at once read neighbouring heads of the same
+// K/V rows.
+template <bool PAGED>
+WATTN_DEVINL DecWork dec_item(const DecParams &p, const PagedTable *pt, int it) {
+  const int split = it % p.n_splits;
+  const int rest = it / p.n_splits;
+  return dec_work<PAGED>(p, pt, split, rest % p.n_heads, rest / p.n_heads);
+}
+
+// Barrier of the four compute warps of the tensor-core path (the producer
+// warp runs ahead and takes no part).
+WATTN_DEVINL void compute_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Issues the TMA loads of the K and V sub-tiles that start at key `key`,
+// each completing on its own barrier.
+template <int KV_DT, bool PAGED>
+WATTN_DEVINL void issue_sub(uint8_t *kdst, uint8_t *vdst, uint64_t *kbar, uint64_t *vbar,
+                            const CUtensorMap &map_k, const CUtensorMap &map_v,
+                            const DecParams &p, const PagedTable *pt, const DecRows &rw,
+                            int head, int key) {
   using G = KvGeom<KV_DT>;
-  constexpr bool kMma = kDecUseMma<Q_DT, KV_DT>;
-  using SmemT = typename std::conditional<kMma, DecSmemMma<KV_DT>, DecSmem<KV_DT>>::type;
+  mbar_arrive_expect_tx(kbar, G::sub_bytes);
+  mbar_arrive_expect_tx(vbar, G::sub_bytes);
+  if constexpr (PAGED) {
+    // Pool rows: (((page * n_layers + layer) * 2 + kv) * n_heads + head) * page_rows + r
+    const int page = pt->pages[rw.row0][key / pt->page_rows];
+    const int r_in = key % pt->page_rows;
+    const int64_t rk =
+        ((((int64_t)page * pt->n_layers + pt->layer) * 2 + 0) * p.n_heads + head) *
+            pt->page_rows + r_in;
+    const int64_t rv = rk + (int64_t)p.n_heads * pt->page_rows;
+#pragma unroll
+    for (int bk = 0; bk < G::blocks; ++bk) {
+      tma_load_2d(kdst + bk * kDecSub * 128, &map_k, kbar, bk * G::block_elems, (int)rk);
+      tma_load_2d(vdst + bk * kDecSub * 128, &map_v, vbar, bk * G::block_elems, (int)rv);
+    }
+  } else {
+#pragma unroll
+    for (int bk = 0; bk < G::blocks; ++bk) {
+      tma_load_4d(kdst + bk * kDecSub * 128, &map_k, kbar, bk * G::block_elems, head, key,
+                  rw.group);
+      tma_load_4d(vdst + bk * kDecSub * 128, &map_v, vbar, bk * G::block_elems, head, key,
+                  rw.group);
+    }
+  }
+}
+
+// Sums the four warps' partial outputs in `red` ([4][kDecRows][64]) and
+// either stores the rows (one split) or writes this split's partial; the
+// last CTA of the (row group, head) to finish then merges every split by
+// log-sum-exp. Called by all threads of the CTA.
+// NAMED: the CTA's compute warps (threads 0..127) call it, synchronising on
+// compute_sync(); otherwise every thread does, on __syncthreads().
+template <typename OutT, bool NAMED>
+__device__ void finish_split(const DecParams &p, const float *red, const float *sm,
+                             const float *sl, int *s_last, const DecRows &rw, int head, int split,
+                             int n_splits) {
+  const int tid = threadIdx.x, nt = NAMED ? kStrWarps * 32 : blockDim.x;
+  const int64_t part_base = (int64_t)rw.row0 * p.n_heads;  // row-major partial index base
+  for (int i = tid; i < rw.nr * 64; i += nt) {
+    const int r = i >> 6, d = i & 63;
+    const float a = red[(0 * kDecRows + r) * 64 + d] + red[(1 * kDecRows + r) * 64 + d] +
+                    red[(2 * kDecRows + r) * 64 + d] + red[(3 * kDecRows + r) * 64 + d];
+    if (n_splits == 1) {
+      store_out<OutT>(p.o, (int64_t)(rw.row0 + r) * p.o_rs + head * 64 + d, a / sl[r]);
+    } else {
+      float *part = p.part + ((part_base + (int64_t)r * p.n_heads + head) * p.n_splits + split) *
+                                 kPartStride;
+      part[d] = a;
+      if (d == 0) {
+        part[64] = sm[r];
+        part[65] = sl[r];
+      }
+    }
+  }
+  if (n_splits == 1) return;
+
+  // Release: the barrier orders every thread's partial before thread 0's
+  // fence, and the fence orders them before the count.
+  if constexpr (NAMED) compute_sync(); else __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    const int prev = atomicAdd(&p.count[rw.cnt_idx], 1);
+    *s_last = (prev == n_splits - 1);
+    if (*s_last) __threadfence();  // acquire: the other splits' partials
+  }
+  if constexpr (NAMED) compute_sync(); else __syncthreads();
+  if (!*s_last) return;
+  for (int i = tid; i < rw.nr * 64; i += nt) {
+    const int r = i >> 6, d = i & 63;
+    const float *part0 =
+        p.part + ((part_base + (int64_t)r * p.n_heads + head) * p.n_splits) * kPartStride;
+    float M = -INFINITY;
+    for (int sp = 0; sp < n_splits; ++sp) M = fmaxf(M, __ldcg(part0 + sp * kPartStride + 64));
+    float L = 0.f, O = 0.f;
+    for (int sp = 0; sp < n_splits; ++sp) {
+      const float w = ex2(__ldcg(part0 + sp * kPartStride + 64) - M);
+      L = fmaf(w, __ldcg(part0 + sp * kPartStride + 65), L);
+      O = fmaf(w, __ldcg(part0 + sp * kPartStride + d), O);
+    }
+    store_out<OutT>(p.o, (int64_t)(rw.row0 + r) * p.o_rs + head * 64 + d, O / L);
+  }
+  if (tid == 0) p.count[rw.cnt_idx] = 0;  // leave the workspace zeroed for the next call
+}
+
+// ---------------------------------------------------------------- tensor-core path
+// Persistent streaming body. CTA b walks items b, b + gridDim.x, ... (the
+// host sizes the grid so each CTA gets the same number of items). Warp
+// kStrWarps (lane 0) fills the ring for all of them in order, running ahead
+// across item boundaries; compute warp w takes keys 16w..16w+15 of every
+// 64-key sub-tile. S = Q K^T and O += P V with mma.sync m16n8k16 (rows = the
+// item's query rows, padded to 16; the scale is applied in f32 to S), online
+// softmax per row in the exp2 domain, then a log-sum-exp merge of the four
+// warps and the split epilogue, while the producer already streams the next
+// item's keys.
+template <int DT>
+WATTN_DEVINL void load_q(uint32_t (&qa)[4][4], const DecParams &p, const DecRows &rw, int head,
+                         int g, int t4) {
+  using T = typename Elem<DT>::T;
+  const uint32_t *qrow = reinterpret_cast<const uint32_t *>(
+      reinterpret_cast<const T *>(p.q) + (int64_t)(rw.row0 + g) * p.q_rs + head * 64);
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks) {
+    qa[ks][0] = g < rw.nr ? qrow[ks * 8 + t4] : 0u;
+    qa[ks][2] = g < rw.nr ? qrow[ks * 8 + 4 + t4] : 0u;
+    qa[ks][1] = qa[ks][3] = 0u;  // rows 8..15 of the tile: beyond the 8 rows of an item
+  }
+}
+
+template <int DT, int OUT_DT, bool PAGED>
+__device__ void decode_stream_body(const CUtensorMap &map_k, const CUtensorMap &map_v,
+                                   const DecParams &p, const PagedTable *pt) {
+  using T = typename Elem<DT>::T;
+  using OutT = typename Elem<OUT_DT>::T;
   extern __shared__ uint8_t dec_smem_raw[];
-  SmemT &s = *reinterpret_cast<SmemT *>(
+  StreamSmem<DT> &s = *reinterpret_cast<StreamSmem<DT> *>(
       (reinterpret_cast<uintptr_t>(dec_smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int split = blockIdx.x, head = blockIdx.y;
-
-  // Rows of this CTA and the physical key range they attend.
-  int row0, nr, kv_lo, kv_hi, group = 0, cnt_idx;
-  if constexpr (PAGED) {
-    row0 = blockIdx.z;
-    nr = 1;
-    kv_lo = pt->kv_lo[row0];
-    kv_hi = pt->kv_hi[row0];
-    cnt_idx = row0 * p.n_heads + head;
-  } else {
-    group = blockIdx.z / p.row_chunks;
-    const int rc = blockIdx.z % p.row_chunks;
-    row0 = group * p.group_size + rc * kDecRows;
-    nr = min(kDecRows, p.group_size - rc * kDecRows);
-    kv_lo = 0;
-    kv_hi = p.t_kv;
-    cnt_idx = blockIdx.z * p.n_heads + head;
-  }
-  const int base = kv_lo & ~(kDecSub - 1);                 // sub-tiles start on 64-row marks
-  const int n_splits = (kv_hi - base + p.chunk - 1) / p.chunk;
-  const int k_beg = base + split * p.chunk;
-  if (k_beg >= kv_hi) return;                              // beyond this row's keys
-  const int n_sub = min(p.chunk, kv_hi - k_beg + kDecSub - 1) / kDecSub;
 
   if (tid == 0) {
-    for (int st = 0; st < n_sub; ++st) {
-      mbar_init(&s.kbar[st], 1);
-      mbar_init(&s.vbar[st], 1);
+    for (int st = 0; st < kStrStages; ++st) {
+      mbar_init(&s.kfull[st], 1);
+      mbar_init(&s.vfull[st], 1);
+      mbar_init(&s.empty[st], kStrWarps);
     }
     s.abort = 0;
     fence_barrier_init();
-    for (int st = 0; st < n_sub; ++st) {
-      const int key = k_beg + st * kDecSub;
-      mbar_arrive_expect_tx(&s.kbar[st], G::sub_bytes);
-      mbar_arrive_expect_tx(&s.vbar[st], G::sub_bytes);
-      if constexpr (PAGED) {
-        // Pool rows: (((page * n_layers + layer) * 2 + kv) * n_heads + head) * page_rows + r
-        const int page = pt->pages[row0][key / pt->page_rows];
-        const int r_in = key % pt->page_rows;
-        const int64_t rk =
-            ((((int64_t)page * pt->n_layers + pt->layer) * 2 + 0) * p.n_heads + head) *
-                pt->page_rows + r_in;
-        const int64_t rv = rk + (int64_t)p.n_heads * pt->page_rows;
-#pragma unroll
-        for (int bk = 0; bk < G::blocks; ++bk) {
-          tma_load_2d(s.k[st] + bk * kDecSub * 128, &map_k, &s.kbar[st], bk * G::block_elems,
-                      (int)rk);
-          tma_load_2d(s.v[st] + bk * kDecSub * 128, &map_v, &s.vbar[st], bk * G::block_elems,
-                      (int)rv);
-        }
-      } else {
-#pragma unroll
-        for (int bk = 0; bk < G::blocks; ++bk) {
-          tma_load_4d(s.k[st] + bk * kDecSub * 128, &map_k, &s.kbar[st], bk * G::block_elems,
-                      head, key, group);
-          tma_load_4d(s.v[st] + bk * kDecSub * 128, &map_v, &s.vbar[st], bk * G::block_elems,
-                      head, key, group);
+  }
+  __syncthreads();
+  volatile int *abort = &s.abort;
+
+  if (warp == kStrWarps) {
+    // ---- producer: one lane refills each stage as the compute warps free it
+    if (lane == 0) {
+      uint32_t c = 0;  // position in the ring, over all items of this CTA
+      for (int it = blockIdx.x; it < p.n_items; it += gridDim.x) {
+        const DecWork w = dec_item<PAGED>(p, pt, it);
+        for (int st = 0; st < w.n_sub; ++st, ++c) {
+          const int stage = c % kStrStages;
+          const uint32_t ph = (c / kStrStages) & 1;
+          if (!mbar_wait(&s.empty[stage], ph ^ 1, abort, p.status,
+                         (2 << 24) | (3 << 16) | ((c & 0xff) << 8)))
+            return;
+          issue_sub<DT, PAGED>(s.k[stage], s.v[stage], &s.kfull[stage], &s.vfull[stage], map_k,
+                               map_v, p, pt, w.rw, w.head, w.k_beg + st * kDecSub);
         }
       }
     }
+    return;  // the producer warp takes no part in the epilogues
   }
 
-  // Per-warp partial outputs, summed over the warps below, in the (now idle)
-  // K buffer: [4 warps][kDecRows][64] floats.
-  float *red = reinterpret_cast<float *>(&s.k[0][0]);
-  if constexpr (kMma) {
-    // ---- tensor-core path. Warp w takes keys 16w..16w+15 of every 64-key
-    // sub-tile. S = Q K^T and O += P V with mma.sync m16n8k16 (rows = query
-    // rows of the group, padded to 16; the scale is applied in f32 to S),
-    // online softmax per row in the exp2 domain on the accumulator
-    // fragments, then the four warps merge by log-sum-exp.
-    const int g = lane >> 2, t4 = lane & 3;
-    volatile int *abort = &s.abort;
-    uint32_t qa[4][4];
-    {
-      const uint32_t *qrow = reinterpret_cast<const uint32_t *>(
-          reinterpret_cast<const QT *>(p.q) + (int64_t)(row0 + g) * p.q_rs + head * 64);
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        qa[ks][0] = g < nr ? qrow[ks * 8 + t4] : 0u;
-        qa[ks][2] = g < nr ? qrow[ks * 8 + 4 + t4] : 0u;
-        qa[ks][1] = qa[ks][3] = 0u;  // rows 8..15 of the tile: beyond the 8 rows of a CTA
-      }
-    }
-    const float c = p.scale_log2;
+  // ---- compute warps
+  const int g = lane >> 2, t4 = lane & 3;
+  const float c = p.scale_log2;
+  const int kb = warp * 16;
+  uint32_t pos = 0;  // position in the ring, as the producer counts it
+  uint32_t qa[4][4], qn[4][4];
+  int q_item = -1;   // item whose query rows qa holds
+  for (int it = blockIdx.x; it < p.n_items; it += gridDim.x) {
+    const DecWork w = dec_item<PAGED>(p, pt, it);
+    if (w.n_sub == 0) continue;  // a paged row with fewer splits than the longest
+    if (q_item != it) load_q<DT>(qa, p, w.rw, w.head, g, t4);
     float m_r = -INFINITY, l_r = 0.f;
     float acc[8][4];
 #pragma unroll
     for (int db = 0; db < 8; ++db) acc[db][0] = acc[db][1] = acc[db][2] = acc[db][3] = 0.f;
-    __syncthreads();  // barrier initialisation visible to every warp
-    const int kb = warp * 16;
-    for (int st = 0; st < n_sub; ++st) {
-      mbar_wait(&s.kbar[st], 0, abort, p.status, (2 << 24) | (1 << 16) | (st << 8));
-      const uint32_t ktile = smem_u32(s.k[st]), vtile = smem_u32(s.v[st]);
+    for (int st = 0; st < w.n_sub; ++st, ++pos) {
+      const int stage = pos % kStrStages;
+      const uint32_t ph = (pos / kStrStages) & 1;
+      mbar_wait(&s.kfull[stage], ph, abort, p.status, (2 << 24) | (1 << 16) | ((pos & 0xff) << 8));
+      const uint32_t ktile = smem_u32(s.k[stage]), vtile = smem_u32(s.v[stage]);
       float sc[2][4];
 #pragma unroll
       for (int nb = 0; nb < 2; ++nb) {
@@ -319,24 +458,24 @@ __device__ void decode_body(const CUtensorMap &map_k, const CUtensorMap &map_v,
           uint32_t r0, r1, r2, r3;
           const int chunk = 4 * ks2 + (lane >> 3);
           ldsm_x4(ktile + key_row * 128 + ((chunk ^ (key_row & 7)) << 4), r0, r1, r2, r3);
-          mma16816<QT>(sc[nb], qa[2 * ks2], r0, r1);
-          mma16816<QT>(sc[nb], qa[2 * ks2 + 1], r2, r3);
+          mma16816<T>(sc[nb], qa[2 * ks2], r0, r1);
+          mma16816<T>(sc[nb], qa[2 * ks2 + 1], r2, r3);
         }
       }
       // Mask keys outside [kv_lo, kv_hi) (row g holds keys 2*t4, 2*t4+1 of each 8).
-      const int key0 = k_beg + st * kDecSub + kb + 2 * t4;
+      const int key0 = w.k_beg + st * kDecSub + kb + 2 * t4;
 #pragma unroll
       for (int nb = 0; nb < 2; ++nb)
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const int key = key0 + nb * 8 + e;
-          if (key < kv_lo || key >= kv_hi) sc[nb][e] = -INFINITY;
+          if (key < w.rw.kv_lo || key >= w.rw.kv_hi) sc[nb][e] = -INFINITY;
         }
       float mx = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
       const float mc = mx * c;
-      if (mc > m_r + 8.0f) {  // lazy rescale, as in the encoder kernel
+      if (mc > m_r + 8.0f) {  // lazy rescale: only when the running max grows by > 2^8
         const float alpha = ex2(m_r - mc);
         l_r *= alpha;
 #pragma unroll
@@ -353,15 +492,15 @@ __device__ void decode_body(const CUtensorMap &map_k, const CUtensorMap &map_v,
 #pragma unroll
         for (int e = 0; e < 2; ++e) pe[nb][e] = ex2(fmaf(sc[nb][e], c, -mu));
       uint32_t pa[4];
-      pa[0] = pack2<QT>(pe[0][0], pe[0][1]);
-      pa[2] = pack2<QT>(pe[1][0], pe[1][1]);
+      pa[0] = pack2<T>(pe[0][0], pe[0][1]);
+      pa[2] = pack2<T>(pe[1][0], pe[1][1]);
       pa[1] = pa[3] = 0u;
       // Normalise by the rounded weights the tensor core uses.
       {
-        const float2 r0 = unpack2<QT>(pa[0]), r2 = unpack2<QT>(pa[2]);
+        const float2 r0 = unpack2<T>(pa[0]), r2 = unpack2<T>(pa[2]);
         l_r += (r0.x + r0.y) + (r2.x + r2.y);
       }
-      mbar_wait(&s.vbar[st], 0, abort, p.status, (2 << 24) | (2 << 16) | (st << 8));
+      mbar_wait(&s.vfull[stage], ph, abort, p.status, (2 << 24) | (2 << 16) | ((pos & 0xff) << 8));
       {
         const int key_row = kb + ((lane >> 3) & 1) * 8 + (lane & 7);
 #pragma unroll
@@ -369,39 +508,87 @@ __device__ void decode_body(const CUtensorMap &map_k, const CUtensorMap &map_v,
           uint32_t r0, r1, r2, r3;
           const int chunk = db2 * 2 + (lane >> 4);
           ldsm_x4_t(vtile + key_row * 128 + ((chunk ^ (key_row & 7)) << 4), r0, r1, r2, r3);
-          mma16816<QT>(acc[2 * db2], pa, r0, r1);
-          mma16816<QT>(acc[2 * db2 + 1], pa, r2, r3);
+          mma16816<T>(acc[2 * db2], pa, r0, r1);
+          mma16816<T>(acc[2 * db2 + 1], pa, r2, r3);
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.empty[stage]);  // this warp is done with the stage
     }
     l_r += __shfl_xor_sync(0xffffffffu, l_r, 1);
     l_r += __shfl_xor_sync(0xffffffffu, l_r, 2);
-    // Merge the four warps (log-sum-exp) into red / s.m / s.l.
-    __syncthreads();  // every warp is done with K: `red` may overwrite it
-    if (t4 == 0 && g < kDecRows) s.wm[warp][g] = m_r;
-    __syncthreads();
-    if (g < nr) {
+
+    // The next item's query rows load while this item's epilogue runs.
+    const int nx = it + gridDim.x;
+    if (nx < p.n_items) {
+      const DecWork wn = dec_item<PAGED>(p, pt, nx);
+      load_q<DT>(qn, p, wn.rw, wn.head, g, t4);
+    }
+
+    // ---- merge the four compute warps (log-sum-exp) into red / s.m / s.l
+    compute_sync();  // the previous item's epilogue is done with red, m, l
+    if (t4 == 0) s.wm[warp][g] = m_r;
+    compute_sync();
+    if (g < w.rw.nr) {
       const float M = fmaxf(fmaxf(s.wm[0][g], s.wm[1][g]), fmaxf(s.wm[2][g], s.wm[3][g]));
-      const float w = (m_r == -INFINITY) ? 0.f : ex2(m_r - M);
+      const float wt = (m_r == -INFINITY) ? 0.f : ex2(m_r - M);
 #pragma unroll
       for (int db = 0; db < 8; ++db)
-        *reinterpret_cast<float2 *>(&red[(warp * kDecRows + g) * 64 + db * 8 + 2 * t4]) =
-            make_float2(acc[db][0] * w, acc[db][1] * w);
+        *reinterpret_cast<float2 *>(&s.red[warp][g][db * 8 + 2 * t4]) =
+            make_float2(acc[db][0] * wt, acc[db][1] * wt);
       if (t4 == 0) {
-        s.wl[warp][g] = l_r * w;
+        s.wl[warp][g] = l_r * wt;
         if (warp == 0) s.m[g] = M;
       }
     }
-    __syncthreads();
-    if (tid < nr) s.l[tid] = s.wl[0][tid] + s.wl[1][tid] + s.wl[2][tid] + s.wl[3][tid];
-    __syncthreads();
-  } else {
+    compute_sync();
+    if (tid < w.rw.nr) s.l[tid] = s.wl[0][tid] + s.wl[1][tid] + s.wl[2][tid] + s.wl[3][tid];
+    compute_sync();
+    finish_split<OutT, true>(p, &s.red[0][0][0], s.m, s.l, &s.last, w.rw, w.head, w.split,
+                             w.n_splits);
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) qa[ks][e] = qn[ks][e];
+    q_item = nx;
+  }
+}
+
+// ---------------------------------------------------------------- CUDA-core path
+template <int Q_DT, int KV_DT, int OUT_DT, bool PAGED>
+__device__ void decode_simt_body(const CUtensorMap &map_k, const CUtensorMap &map_v,
+                                 const DecParams &p, const PagedTable *pt) {
+  using QT = typename Elem<Q_DT>::T;
+  using OutT = typename Elem<OUT_DT>::T;
+  extern __shared__ uint8_t dec_smem_raw[];
+  DecSmem<KV_DT> &s = *reinterpret_cast<DecSmem<KV_DT> *>(
+      (reinterpret_cast<uintptr_t>(dec_smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const DecWork w = dec_work<PAGED>(p, pt, blockIdx.x, blockIdx.y, blockIdx.z);
+  if (w.n_sub == 0) return;  // beyond this row's keys
+  const DecRows &rw = w.rw;
+  const int nr = rw.nr, head = w.head, split = w.split, n_splits = w.n_splits;
+  const int k_beg = w.k_beg, n_sub = w.n_sub;
+
+  if (tid == 0) {
+    for (int st = 0; st < n_sub; ++st) {
+      mbar_init(&s.kbar[st], 1);
+      mbar_init(&s.vbar[st], 1);
+    }
+    s.abort = 0;
+    fence_barrier_init();
+    for (int st = 0; st < n_sub; ++st)
+      issue_sub<KV_DT, PAGED>(s.k[st], s.v[st], &s.kbar[st], &s.vbar[st], map_k, map_v, p, pt,
+                              rw, head, k_beg + st * kDecSub);
+  }
+
   // Query rows, pre-scaled into the exp2 domain.
   for (int i = tid; i < kDecRows * 64; i += kDecThreads) {
     const int r = i >> 6, d = i & 63;
     float x = 0.f;
     if (r < nr)
-      x = to_f32(reinterpret_cast<const QT *>(p.q)[(int64_t)(row0 + r) * p.q_rs + head * 64 + d]);
+      x = to_f32(
+          reinterpret_cast<const QT *>(p.q)[(int64_t)(rw.row0 + r) * p.q_rs + head * 64 + d]);
     s.q[r][d] = x * p.scale_log2;
   }
   __syncthreads();
@@ -414,7 +601,7 @@ __device__ void decode_body(const CUtensorMap &map_k, const CUtensorMap &map_v,
     float dot[kDecRows];
     half_dots<KV_DT>(s.k[st], krow, half, s.q, nr, dot);
     const int key = k_beg + st * kDecSub + krow;
-    const bool valid = key >= kv_lo && key < kv_hi;
+    const bool valid = key >= rw.kv_lo && key < rw.kv_hi;
 #pragma unroll
     for (int r = 0; r < kDecRows; ++r) {
       const float full = dot[r] + __shfl_xor_sync(0xffffffffu, dot[r], 1);
@@ -465,66 +652,25 @@ __device__ void decode_body(const CUtensorMap &map_k, const CUtensorMap &map_v,
       }
     }
   }
-  // Cross-warp sum through the (now idle) K buffer.
+  // Cross-warp sum through the K buffer, idle since the barrier after the scores.
+  float *red = reinterpret_cast<float *>(&s.k[0][0]);
 #pragma unroll
   for (int r = 0; r < kDecRows; ++r)
-    if (r < nr) *reinterpret_cast<float2 *>(&red[(warp * kDecRows + r) * 64 + 2 * lane]) =
-        make_float2(acc[r][0], acc[r][1]);
+    if (r < nr)
+      *reinterpret_cast<float2 *>(&red[(warp * kDecRows + r) * 64 + 2 * lane]) =
+          make_float2(acc[r][0], acc[r][1]);
   __syncthreads();
-
-  }
-
-  const int64_t part_base = (int64_t)row0 * p.n_heads;  // row-major partial index base
-  for (int i = tid; i < nr * 64; i += kDecThreads) {
-    const int r = i >> 6, d = i & 63;
-    const float a = red[(0 * kDecRows + r) * 64 + d] + red[(1 * kDecRows + r) * 64 + d] +
-                    red[(2 * kDecRows + r) * 64 + d] + red[(3 * kDecRows + r) * 64 + d];
-    if (n_splits == 1) {
-      store_out<OutT>(p.o, (int64_t)(row0 + r) * p.o_rs + head * 64 + d, a / s.l[r]);
-    } else {
-      float *part = p.part + ((part_base + (int64_t)r * p.n_heads + head) * p.n_splits + split) *
-                                 kPartStride;
-      part[d] = a;
-      if (d == 0) {
-        part[64] = s.m[r];
-        part[65] = s.l[r];
-      }
-    }
-  }
-  if (n_splits == 1) return;
-
-  // ---- last CTA of this (row group, head) merges the splits (log-sum-exp)
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    const int prev = atomicAdd(&p.count[cnt_idx], 1);
-    s.last = (prev == n_splits - 1);
-  }
-  __syncthreads();
-  if (!s.last) return;
-  __threadfence();
-  for (int i = tid; i < nr * 64; i += kDecThreads) {
-    const int r = i >> 6, d = i & 63;
-    const float *part0 =
-        p.part + ((part_base + (int64_t)r * p.n_heads + head) * p.n_splits) * kPartStride;
-    float M = -INFINITY;
-    for (int sp = 0; sp < n_splits; ++sp) M = fmaxf(M, __ldcg(part0 + sp * kPartStride + 64));
-    float L = 0.f, O = 0.f;
-    for (int sp = 0; sp < n_splits; ++sp) {
-      const float w = ex2(__ldcg(part0 + sp * kPartStride + 64) - M);
-      L = fmaf(w, __ldcg(part0 + sp * kPartStride + 65), L);
-      O = fmaf(w, __ldcg(part0 + sp * kPartStride + d), O);
-    }
-    store_out<OutT>(p.o, (int64_t)(row0 + r) * p.o_rs + head * 64 + d, O / L);
-  }
-  if (tid == 0) p.count[cnt_idx] = 0;  // leave the workspace zeroed for the next call
+  finish_split<OutT, false>(p, red, s.m, s.l, &s.last, rw, head, split, n_splits);
 }
+
+template <int Q_DT, int KV_DT>
+constexpr bool kDecStream = KV_DT != WATTN_F32 && Q_DT == KV_DT;
 
 template <int Q_DT, int KV_DT, int OUT_DT>
 __global__ void __launch_bounds__(kDecThreads)
     decode_dense_kernel(const __grid_constant__ CUtensorMap map_k,
                         const __grid_constant__ CUtensorMap map_v, const DecParams p) {
-  decode_body<Q_DT, KV_DT, OUT_DT, false>(map_k, map_v, p, nullptr);
+  decode_simt_body<Q_DT, KV_DT, OUT_DT, false>(map_k, map_v, p, nullptr);
 }
 
 template <int Q_DT, int KV_DT, int OUT_DT>
@@ -532,12 +678,22 @@ __global__ void __launch_bounds__(kDecThreads)
     decode_paged_kernel(const __grid_constant__ CUtensorMap map_k,
                         const __grid_constant__ CUtensorMap map_v, const DecParams p,
                         const __grid_constant__ PagedTable pt) {
-  decode_body<Q_DT, KV_DT, OUT_DT, true>(map_k, map_v, p, &pt);
+  decode_simt_body<Q_DT, KV_DT, OUT_DT, true>(map_k, map_v, p, &pt);
 }
 
-template <int Q_DT, int KV_DT> constexpr int dec_smem_bytes() {
-  return (kDecUseMma<Q_DT, KV_DT> ? (int)sizeof(DecSmemMma<KV_DT>) : (int)sizeof(DecSmem<KV_DT>)) +
-         1024;
+template <int DT, int OUT_DT>
+__global__ void __launch_bounds__(kStrThreads)
+    decode_stream_dense_kernel(const __grid_constant__ CUtensorMap map_k,
+                               const __grid_constant__ CUtensorMap map_v, const DecParams p) {
+  decode_stream_body<DT, OUT_DT, false>(map_k, map_v, p, nullptr);
+}
+
+template <int DT, int OUT_DT>
+__global__ void __launch_bounds__(kStrThreads)
+    decode_stream_paged_kernel(const __grid_constant__ CUtensorMap map_k,
+                               const __grid_constant__ CUtensorMap map_v, const DecParams p,
+                               const __grid_constant__ PagedTable pt) {
+  decode_stream_body<DT, OUT_DT, true>(map_k, map_v, p, &pt);
 }
 
 template <typename K>
@@ -548,40 +704,47 @@ int set_smem(K kern, int bytes) {
   return WATTN_OK;
 }
 
-template <int Q_DT, int KV_DT, int OUT_DT>
-int launch_dense_typed(const CUtensorMap &mk, const CUtensorMap &mv, const DecParams &p,
-                       int n_groups, cudaStream_t stream) {
-  auto kern = decode_dense_kernel<Q_DT, KV_DT, OUT_DT>;
-  const int smem = dec_smem_bytes<Q_DT, KV_DT>();
-  int rc = set_smem(kern, smem);
-  if (rc != WATTN_OK) return rc;
-  dim3 grid(p.n_splits, p.n_heads, n_groups * p.row_chunks);
-  kern<<<grid, kDecThreads, smem, stream>>>(mk, mv, p);
-  return check_launch("decode_dense");
-}
-
-template <int Q_DT, int KV_DT, int OUT_DT>
-int launch_paged_typed(const CUtensorMap &mk, const CUtensorMap &mv, const DecParams &p,
-                       const PagedTable &pt, int max_splits, cudaStream_t stream) {
-  auto kern = decode_paged_kernel<Q_DT, KV_DT, OUT_DT>;
-  const int smem = dec_smem_bytes<Q_DT, KV_DT>();
-  int rc = set_smem(kern, smem);
-  if (rc != WATTN_OK) return rc;
-  dim3 grid(max_splits, p.n_heads, pt.n_rows);
-  kern<<<grid, kDecThreads, smem, stream>>>(mk, mv, p, pt);
-  return check_launch("decode_paged");
+// Grid: (splits, heads, row groups x row chunks) dense; (splits, heads, rows) paged.
+template <int Q_DT, int KV_DT, int OUT_DT, bool PAGED>
+int launch_typed(const CUtensorMap &mk, const CUtensorMap &mv, const DecParams &p,
+                 const PagedTable *pt, dim3 grid, cudaStream_t stream) {
+  if constexpr (kDecStream<Q_DT, KV_DT>) {
+    constexpr int smem = (int)sizeof(StreamSmem<KV_DT>) + 1024;
+    if constexpr (PAGED) {
+      auto kern = decode_stream_paged_kernel<KV_DT, OUT_DT>;
+      int rc = set_smem(kern, smem);
+      if (rc != WATTN_OK) return rc;
+      kern<<<grid, kStrThreads, smem, stream>>>(mk, mv, p, *pt);
+    } else {
+      auto kern = decode_stream_dense_kernel<KV_DT, OUT_DT>;
+      int rc = set_smem(kern, smem);
+      if (rc != WATTN_OK) return rc;
+      kern<<<grid, kStrThreads, smem, stream>>>(mk, mv, p);
+    }
+  } else {
+    constexpr int smem = (int)sizeof(DecSmem<KV_DT>) + 1024;
+    if constexpr (PAGED) {
+      auto kern = decode_paged_kernel<Q_DT, KV_DT, OUT_DT>;
+      int rc = set_smem(kern, smem);
+      if (rc != WATTN_OK) return rc;
+      kern<<<grid, kDecThreads, smem, stream>>>(mk, mv, p, *pt);
+    } else {
+      auto kern = decode_dense_kernel<Q_DT, KV_DT, OUT_DT>;
+      int rc = set_smem(kern, smem);
+      if (rc != WATTN_OK) return rc;
+      kern<<<grid, kDecThreads, smem, stream>>>(mk, mv, p);
+    }
+  }
+  return check_launch(PAGED ? "decode_paged" : "decode_dense");
 }
 
 // Dispatch over (q, kv, out) element types.
 template <bool PAGED>
 int dispatch(int q_dt, int kv_dt, int out_dt, const CUtensorMap &mk, const CUtensorMap &mv,
-             const DecParams &p, int n_groups, const PagedTable *pt, int max_splits,
-             cudaStream_t stream) {
-#define WATTN_DEC_CASE(QD, KD, OD)                                                     \
-  if (q_dt == QD && kv_dt == KD && out_dt == OD) {                                     \
-    if constexpr (PAGED) return launch_paged_typed<QD, KD, OD>(mk, mv, p, *pt, max_splits, stream); \
-    else return launch_dense_typed<QD, KD, OD>(mk, mv, p, n_groups, stream);          \
-  }
+             const DecParams &p, const PagedTable *pt, dim3 grid, cudaStream_t stream) {
+#define WATTN_DEC_CASE(QD, KD, OD)                                       \
+  if (q_dt == QD && kv_dt == KD && out_dt == OD)                         \
+    return launch_typed<QD, KD, OD, PAGED>(mk, mv, p, pt, grid, stream);
 #define WATTN_DEC_KV(QD, OD)              \
   WATTN_DEC_CASE(QD, WATTN_F32, OD)       \
   WATTN_DEC_CASE(QD, WATTN_F16, OD)       \
@@ -599,9 +762,24 @@ int dispatch(int q_dt, int kv_dt, int out_dt, const CUtensorMap &mk, const CUten
   return set_error(WATTN_ERR_INVALID, "decode: unsupported dtype combination");
 }
 
-int chunk_for(int kv_dtype, int ctas_per_chunk_unit, int t_kv) {
-  // Largest chunk (<= 256 keys, 128 for f32 K/V to fit shared memory) that
-  // still gives >= ~4 waves of CTAs on 148 SMs.
+bool uses_stream(int q_dtype, int kv_dtype) {
+  return kv_dtype != WATTN_F32 && q_dtype == kv_dtype;
+}
+
+// Keys per split. Tensor-core path: as many splits as it takes to give
+// every resident CTA an item (none where there are already enough items),
+// each split at least kStrMinSubs sub-tiles where the keys allow, the splits
+// of a row equal to within a sub-tile. CUDA-core path: the largest chunk
+// (<= 256 keys, 128 for f32 K/V to fit shared memory) that still gives
+// >= ~4 waves of CTAs on 148 SMs.
+int chunk_for(int q_dtype, int kv_dtype, int ctas_per_chunk_unit, int t_kv) {
+  const int subs = std::max(1, (t_kv + kDecSub - 1) / kDecSub);
+  if (uses_stream(q_dtype, kv_dtype)) {
+    const long long units = std::max(1, ctas_per_chunk_unit);
+    int splits = (int)std::min<long long>((kStrSlots + units - 1) / units, subs);
+    splits = std::max(1, std::min(splits, subs / kStrMinSubs));
+    return ((subs + splits - 1) / splits) * kDecSub;
+  }
   const int max_chunk = (kv_dtype == WATTN_F32 ? 2 : kDecMaxSubs) * kDecSub;
   int chunk = max_chunk;
   while (chunk > kDecSub) {
@@ -612,14 +790,21 @@ int chunk_for(int kv_dtype, int ctas_per_chunk_unit, int t_kv) {
   return chunk;
 }
 
-size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+// Persistent grid of the tensor-core path: the fewest CTAs that give every
+// CTA the same number of items (to within one) with at most kStrSlots CTAs
+// per round of items.
+int stream_grid(long long items) {
+  const long long per_cta = (items + kStrSlots - 1) / kStrSlots;
+  return (int)((items + per_cta - 1) / per_cta);
+}
 
 }  // namespace
 
-DecodePlan plan_decode(int n_groups, int group_size, int t_kv, int n_heads, int kv_dtype) {
+DecodePlan plan_decode(int n_groups, int group_size, int t_kv, int n_heads, int q_dtype,
+                       int kv_dtype) {
   DecodePlan pl;
   pl.row_chunks = (group_size + kDecRows - 1) / kDecRows;
-  pl.chunk = chunk_for(kv_dtype, n_groups * pl.row_chunks * n_heads, t_kv);
+  pl.chunk = chunk_for(q_dtype, kv_dtype, n_groups * pl.row_chunks * n_heads, t_kv);
   pl.n_splits = t_kv > 0 ? (t_kv + pl.chunk - 1) / pl.chunk : 1;
   const size_t rows = (size_t)n_groups * group_size;
   pl.workspace_bytes = kCounterBytes + rows * n_heads * pl.n_splits * kPartStride * sizeof(float);
@@ -630,7 +815,7 @@ int launch_decode(const void *q, const void *k, const void *v, void *o, int q_dt
                   int kv_dtype, int out_dtype, int n_groups, int group_size, int t_kv,
                   int n_heads, int64_t q_rs, int64_t kv_rs, int64_t kv_gs, int64_t o_rs,
                   float scale, void *workspace, size_t workspace_bytes, cudaStream_t stream) {
-  const DecodePlan pl = plan_decode(n_groups, group_size, t_kv, n_heads, kv_dtype);
+  const DecodePlan pl = plan_decode(n_groups, group_size, t_kv, n_heads, q_dtype, kv_dtype);
   if (pl.n_splits > 1 && workspace_bytes < pl.workspace_bytes)
     return set_error(WATTN_ERR_INVALID, "decode: workspace of %zu bytes, %zu needed",
                      workspace_bytes, pl.workspace_bytes);
@@ -665,7 +850,11 @@ int launch_decode(const void *q, const void *k, const void *v, void *o, int q_dt
   p.part = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(workspace) + kCounterBytes);
   p.status = device_status_ptr();
   if (p.status == nullptr) return WATTN_ERR_CUDA;
-  return dispatch<false>(q_dtype, kv_dtype, out_dtype, mk, mv, p, n_groups, nullptr, 0, stream);
+  p.n_items = pl.n_splits * n_heads * n_groups * pl.row_chunks;
+  const dim3 grid = uses_stream(q_dtype, kv_dtype)
+                        ? dim3(stream_grid(p.n_items))
+                        : dim3(pl.n_splits, n_heads, n_groups * pl.row_chunks);
+  return dispatch<false>(q_dtype, kv_dtype, out_dtype, mk, mv, p, nullptr, grid, stream);
 }
 
 // Paged launch, used by the KV cache (kv_cache.cu).
@@ -683,7 +872,7 @@ int launch_decode_paged(const CUtensorMap &map_k, const CUtensorMap &map_v, cons
   p.t_kv = 0;
   p.n_heads = n_heads;
   p.row_chunks = 1;
-  p.chunk = chunk_for(kv_dtype, pt.n_rows * n_heads, max_keys);
+  p.chunk = chunk_for(q_dtype, kv_dtype, pt.n_rows * n_heads, max_keys);
   p.n_splits = (max_keys + p.chunk - 1) / p.chunk;  // upper bound; rows use their own
   p.scale_log2 = scale * 1.4426950408889634f;
   const size_t need =
@@ -699,8 +888,11 @@ int launch_decode_paged(const CUtensorMap &map_k, const CUtensorMap &map_v, cons
   p.part = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(workspace) + kCounterBytes);
   p.status = device_status_ptr();
   if (p.status == nullptr) return WATTN_ERR_CUDA;
-  return dispatch<true>(q_dtype, kv_dtype, out_dtype, map_k, map_v, p, 0, &pt, p.n_splits,
-                        stream);
+  p.n_items = p.n_splits * n_heads * pt.n_rows;
+  const dim3 grid = !uses_stream(q_dtype, kv_dtype) ? dim3(p.n_splits, n_heads, pt.n_rows)
+                    : kStrPagedPersist              ? dim3(stream_grid(p.n_items))
+                                                    : dim3(p.n_items);
+  return dispatch<true>(q_dtype, kv_dtype, out_dtype, map_k, map_v, p, &pt, grid, stream);
 }
 
 size_t paged_workspace_bytes(int n_rows, int n_heads, int max_keys) {

@@ -87,7 +87,7 @@ extern "C" int wattn_decode_fwd_noalloc(const void *q, const void *k, const void
   if (t_kv == 0)
     return launch_zero_rows(o, out_dtype, 1, n_groups * group_size, n_heads * kHeadDim,
                             o_row_stride, 0, st);
-  const DecodePlan pl = plan_decode(n_groups, group_size, t_kv, n_heads, kv_dtype);
+  const DecodePlan pl = plan_decode(n_groups, group_size, t_kv, n_heads, q_dtype, kv_dtype);
   if (pl.n_splits > 1 && pl.workspace_bytes > kNoAllocScratchBytes)
     return set_error(WATTN_ERR_RANGE,
                      "decode_fwd_noalloc: this call needs %zu bytes of scratch; the built-in "

@@ -63,7 +63,8 @@ struct DecodePlan {
   int row_chunks; // ceil(group_size / rows per CTA)
   size_t workspace_bytes;
 };
-DecodePlan plan_decode(int n_groups, int group_size, int t_kv, int n_heads, int kv_dtype);
+DecodePlan plan_decode(int n_groups, int group_size, int t_kv, int n_heads, int q_dtype,
+                       int kv_dtype);
 int launch_decode(const void *q, const void *k, const void *v, void *o, int q_dtype,
                   int kv_dtype, int out_dtype, int n_groups, int group_size, int t_kv,
                   int n_heads, int64_t q_rs, int64_t kv_rs, int64_t kv_gs, int64_t o_rs,
