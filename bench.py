@@ -480,11 +480,12 @@ def main():
     ap.add_argument("--no-extras", action="store_true", help="headline only")
     ap.add_argument("--only", choices=["all", "enc", "dec", "xdec"], default="all",
                     help="profiling aid: run one workload only")
-    ap.add_argument("--layers", type=int, default=None, help="profiling aid: config 3 layers")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="profiling aid: layers of the workload --only selects (config 3 by default)")
     ap.add_argument("--batch", type=int, default=None, help="profiling aid: config 3 batch")
     a = ap.parse_args()
     if a.layers:
-        C3["layers"] = a.layers
+        {"dec": C5, "xdec": C4}.get(a.only, C3)["layers"] = a.layers
     if a.batch:
         C3["batch"] = a.batch
     world = int(os.environ.get("WORLD_SIZE", "1"))

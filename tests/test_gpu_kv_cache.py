@@ -128,6 +128,20 @@ def test_beam_history(W, oracle, dtype):
     assert h.dev.stats()[0] == 0
 
 
+@pytest.mark.parametrize("dtype", [1, 2], ids=["f16", "bf16"])
+def test_ragged_batch_many_rows(W, oracle, dtype):
+    """Many slots of ragged lengths at 20 heads: one attend call spans several
+    kernel launches (more rows than one launch's table holds), entries are
+    reordered by length inside each launch and every CTA of the persistent
+    grid serves several (row, head) items."""
+    rng = np.random.default_rng(7)
+    h = Harness(W, oracle, dtype, n_layers=1, n_slots=40, n_heads=20, max_ctx=448, page_rows=64)
+    slots = list(range(40))
+    h.step(slots, [int(x) for x in rng.integers(1, 300, size=40)])  # ragged prefill
+    h.step(slots, [1] * 40)                                           # one decode step
+    h.step(slots[::3], [int(x) for x in rng.integers(1, 12, size=len(slots[::3]))])
+
+
 def test_cache_errors(W):
     c = W.DeviceKvCache(1, 2, 2, 128)
     with pytest.raises(W.WattnError) as e:

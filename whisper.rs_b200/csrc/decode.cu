@@ -47,13 +47,17 @@ constexpr int kStrWarps = 4;       // compute warps; one more warp issues the lo
 constexpr int kStrThreads = (kStrWarps + 1) * 32;
 constexpr int kStrSlots = 148 * 3; // resident tensor-core CTAs on a B200: three per SM
 constexpr int kStrMinSubs = 4;     // sub-tiles per split below which no further split is made
-constexpr bool kStrPagedPersist = false;  // paged rows vary in length: one item per CTA
+constexpr bool kStrPagedPersist = true;  // paged entries come sorted by length
 // Workspace layout, the same for every call: [counters][partials]. The
 // counter region has a fixed size, so partials written by one call can never
 // land where a later call of another shape keeps its counters; every call
 // leaves the counters it used at zero.
 constexpr size_t kCounterBytes = (size_t)kMaxSplitCounters * sizeof(int);
 static_assert(kDecSub == kDecSubRows, "paged sub-tiles and TMA boxes must agree");
+// Paged kernels take two tensor maps, DecParams (< 128 bytes) and the table
+// by value; CUDA 12.1+ allows 32764 bytes of kernel parameters.
+static_assert(2 * sizeof(CUtensorMap) + 128 + sizeof(PagedTable) <= 32764,
+              "paged kernel parameters exceed the 32764-byte limit");
 
 namespace {
 
@@ -217,6 +221,7 @@ WATTN_DEVINL void store_out(void *o, int64_t off, float x) {
 // they attend; `cnt_idx` is the item's split counter.
 struct DecRows {
   int row0, nr, kv_lo, kv_hi, group, cnt_idx;
+  int entry;  // paged: the item's entry in the PagedTable
 };
 
 // One work item: split `split` of the keys of (row chunk / paged row z,
@@ -233,7 +238,8 @@ WATTN_DEVINL DecWork dec_work(const DecParams &p, const PagedTable *pt, int spli
   DecWork w;
   DecRows &r = w.rw;
   if constexpr (PAGED) {
-    r.row0 = z;
+    r.entry = z;
+    r.row0 = pt->row_of[z];
     r.nr = 1;
     r.kv_lo = pt->kv_lo[z];
     r.kv_hi = pt->kv_hi[z];
@@ -245,6 +251,7 @@ WATTN_DEVINL DecWork dec_work(const DecParams &p, const PagedTable *pt, int spli
     r.nr = min(kDecRows, p.group_size - rc * kDecRows);
     r.kv_lo = 0;
     r.kv_hi = p.t_kv;
+    r.entry = 0;
   }
   r.cnt_idx = z * p.n_heads + head;
   w.head = head;
@@ -282,7 +289,7 @@ WATTN_DEVINL void issue_sub(uint8_t *kdst, uint8_t *vdst, uint64_t *kbar, uint64
   mbar_arrive_expect_tx(vbar, G::sub_bytes);
   if constexpr (PAGED) {
     // Pool rows: (((page * n_layers + layer) * 2 + kv) * n_heads + head) * page_rows + r
-    const int page = pt->pages[rw.row0][key / pt->page_rows];
+    const int page = pt->pages[rw.entry][key / pt->page_rows];
     const int r_in = key % pt->page_rows;
     const int64_t rk =
         ((((int64_t)page * pt->n_layers + pt->layer) * 2 + 0) * p.n_heads + head) *

@@ -515,7 +515,7 @@ int wattn_kv_attend(wattn_kv_cache *c, int layer, const int *slots, const int *n
                      workspace_bytes, need);
   }
 
-  static thread_local PagedTable pt;  // ~18 KB: keep it off the stack
+  static thread_local PagedTable pt, sorted;  // ~29 KB each: keep them off the stack
   pt.layer = layer;
   pt.n_layers = c->n_layers;
   pt.page_rows = c->page_rows;
@@ -526,8 +526,25 @@ int wattn_kv_attend(wattn_kv_cache *c, int layer, const int *slots, const int *n
     if (pt.n_rows == 0) return WATTN_OK;
     const uint8_t *qp = (const uint8_t *)q + (int64_t)row_base * q_row_stride * es_q;
     uint8_t *op = (uint8_t *)o + (int64_t)row_base * o_row_stride * es_o;
+    // Entries by descending key count (stable), each keeping its own row.
+    int idx[kPagedMaxRows];
+    for (int r = 0; r < pt.n_rows; ++r) idx[r] = r;
+    std::stable_sort(idx, idx + pt.n_rows, [&](int a, int b) {
+      return pt.kv_hi[a] - pt.kv_lo[a] > pt.kv_hi[b] - pt.kv_lo[b];
+    });
+    sorted.n_rows = pt.n_rows;
+    sorted.layer = pt.layer;
+    sorted.n_layers = pt.n_layers;
+    sorted.page_rows = pt.page_rows;
+    for (int e = 0; e < pt.n_rows; ++e) {
+      const int r = idx[e];
+      sorted.row_of[e] = r;
+      sorted.kv_lo[e] = pt.kv_lo[r];
+      sorted.kv_hi[e] = pt.kv_hi[r];
+      for (int pi = 0; pi < kPagedMaxPages; ++pi) sorted.pages[e][pi] = pt.pages[r][pi];
+    }
     int rc = launch_decode_paged(c->map, c->map, qp, op, q_dtype, c->dtype, out_dtype, c->n_heads,
-                                 q_row_stride, o_row_stride, scale, pt, max_keys, workspace,
+                                 q_row_stride, o_row_stride, scale, sorted, max_keys, workspace,
                                  workspace_bytes, st);
     row_base += pt.n_rows;
     pt.n_rows = 0;

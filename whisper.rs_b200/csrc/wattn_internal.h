@@ -72,15 +72,19 @@ int launch_decode(const void *q, const void *k, const void *v, void *o, int q_dt
 
 // ----------------------------------------------------------- paged decode
 constexpr int kDecSubRows = 64;     // keys per decode sub-tile (TMA box rows)
-constexpr int kPagedMaxRows = 256;  // query rows per paged launch
+constexpr int kPagedMaxRows = 384;  // query rows per paged launch
 constexpr int kPagedMaxPages = 16;  // pages per row in one launch
 
 // Kernel-parameter table of one paged decode launch (passed by value, about
-// 18 KB): for each query row, its slot's pages and the physical key range
-// [kv_lo, kv_hi) it attends.
+// 29 KB, within the 32 KB kernel-parameter limit): for each entry, the query
+// / output row it serves (row_of, relative to the launch's first row), that
+// row's slot pages and the physical key range [kv_lo, kv_hi) it attends.
+// Entries are sorted by descending key count, so the items a persistent grid
+// deals out round by round are of similar length.
 struct PagedTable {
   int n_rows;
   int layer, n_layers, page_rows;
+  int row_of[kPagedMaxRows];
   int kv_lo[kPagedMaxRows];
   int kv_hi[kPagedMaxRows];
   int pages[kPagedMaxRows][kPagedMaxPages];
