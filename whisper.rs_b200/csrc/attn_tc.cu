@@ -4,9 +4,13 @@
 // (crates/tensor/src/ops/attention.rs:111-241) for f16 / bf16 inputs with
 // f32 accumulation. Same function, B200 structure:
 //
-//   * one CTA owns two 128-row query tiles of one (utterance, head); each
-//     tile has its own softmax warpgroup, so while one warpgroup turns S into
-//     P the tensor cores work on the other tile;
+//   * a persistent grid of one CTA per SM walks work units of two 128-row
+//     query tiles of one (utterance, head); each tile has its own softmax
+//     warpgroup, so while one warpgroup turns S into P the tensor cores work
+//     on the other tile. Every barrier phase, the K/V ring and the TMEM
+//     buffers carry over from unit to unit, so the next unit's Q and first
+//     K/V tiles load and its first scores are computed while the current
+//     unit's last softmax and epilogue run;
 //   * a TMA warp streams 128-key K and V tiles through a 3-deep ring in
 //     shared memory (128-byte swizzle, the layout UMMA reads directly);
 //   * an MMA warp issues tcgen05.mma: S = Q K^T (M=128, N=128, K=64) into
@@ -30,6 +34,9 @@
 #include "wattn_common.cuh"
 #include "wattn_internal.h"
 
+#include <algorithm>
+#include <climits>
+
 namespace wattn {
 namespace {
 
@@ -48,17 +55,24 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units
 // faster setting measured so far on B200).
 constexpr int kFmaExp2Every = 0;
 
+// Whether exponential pair i is computed on the FMA pipe.
+WATTN_DEVINL constexpr bool fma_exp2_slot(int i) {
+  constexpr int every = kFmaExp2Every > 0 ? kFmaExp2Every : 1;
+  return kFmaExp2Every > 0 && i % every == every - 1;
+}
+
 struct Smem {
   uint8_t q[kTiles][kTileBytes];
   uint8_t k[kStages][kTileBytes];
   uint8_t v[kStages][kTileBytes];
-  uint64_t q_full;
+  uint64_t q_full, q_empty;  // Q tiles loaded / the unit's last S done (Q may be replaced)
   uint64_t k_full[kStages], k_empty[kStages];
   uint64_t v_full[kStages], v_empty[kStages];
   uint64_t s_full[kTiles];  // S(t, j) in TMEM (MMA commit)
   uint64_t s_free[kTiles];  // S(t, j) read into registers: S(t, j+1) may overwrite it
   uint64_t p_full[kTiles];  // P(t, j) in TMEM and O(t) rescaled (softmax arrivals)
   uint64_t o_done[kTiles];  // PV(t, j) complete: P(t, j+1) may be written (MMA commit)
+  uint64_t o_free[kTiles];  // the epilogue has read O(t): the next unit may overwrite it
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -71,6 +85,7 @@ struct Params {
   void *o;
   int64_t o_rs, o_bs;
   int t_q, t_kv;
+  int n_qblk, n_heads, n_units;  // work units: (query block, head, utterance)
   float scale_log2;  // scale * log2(e)
   int causal, q_pos_offset;
   int *status;
@@ -98,6 +113,25 @@ WATTN_DEVINL void store_row(OutT *dst, const uint32_t (&o)[2][32], float inv) {
   }
 }
 
+// Work unit u of the persistent grid: query block fastest, then head, then
+// utterance, so the units running at once share their K/V rows in L2.
+struct Unit {
+  int q0, head, b, n_tiles, nkv;
+};
+
+WATTN_DEVINL Unit unit_of(const Params &p, int u) {
+  Unit w;
+  const int qb = u % p.n_qblk, rest = u / p.n_qblk;
+  w.head = rest % p.n_heads;
+  w.b = rest / p.n_heads;
+  w.q0 = qb * (kBM * kTiles);
+  w.n_tiles = min(kTiles, (p.t_q - w.q0 + kBM - 1) / kBM);
+  int kv_end = p.t_kv;
+  if (p.causal) kv_end = min(kv_end, min(w.q0 + kBM * kTiles, p.t_q) + p.q_pos_offset);
+  w.nkv = kv_end > 0 ? (kv_end + kBN - 1) / kBN : 0;
+  return w;
+}
+
 template <int IN_DT, int OUT_DT>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_q,
@@ -109,15 +143,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   Smem &s = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                       ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int head = blockIdx.y, b = blockIdx.z;
-  const int q0 = blockIdx.x * (kBM * kTiles);
-  const int n_tiles = min(kTiles, (p.t_q - q0 + kBM - 1) / kBM);
-  int kv_end = p.t_kv;
-  if (p.causal) kv_end = min(kv_end, min(q0 + kBM * kTiles, p.t_q) + p.q_pos_offset);
-  const int nkv = kv_end > 0 ? (kv_end + kBN - 1) / kBN : 0;
 
   if (threadIdx.x == 0) {
     mbar_init(&s.q_full, 1);
+    mbar_init(&s.q_empty, 1);
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&s.k_full[i], 1);
       mbar_init(&s.k_empty[i], 1);
@@ -129,6 +158,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s.s_free[t], kBM);
       mbar_init(&s.p_full[t], kBM);
       mbar_init(&s.o_done[t], 1);
+      mbar_init(&s.o_free[t], kBM);
     }
     mbar_init(&s.drain, 1);
     s.abort = 0;
@@ -147,25 +177,43 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kTmaWarp) {
     // ---------------------------------------------------------- TMA producer
-    if (lane == 0 && nkv > 0) {
+    if (lane == 0) {
       tma_prefetch_desc(&map_q);
       tma_prefetch_desc(&map_k);
       tma_prefetch_desc(&map_v);
-      mbar_arrive_expect_tx(&s.q_full, n_tiles * kTileBytes);
-      for (int t = 0; t < n_tiles; ++t)
-        tma_load_4d(s.q[t], &map_q, &s.q_full, 0, head, q0 + t * kBM, b);
-      int last_k = -1, last_v = -1;  // last tiles issued, for the wind-down
-      for (int j = 0; j < nkv; ++j) {
-        const int st = j % kStages;
-        const uint32_t ph = (j / kStages) & 1;
-        if (!mbar_wait(&s.k_empty[st], ph ^ 1, abort, p.status, TC_SITE(1, 1, j))) break;
-        mbar_arrive_expect_tx(&s.k_full[st], kTileBytes);
-        tma_load_4d(s.k[st], &map_k, &s.k_full[st], 0, head, j * kBN, b);
-        last_k = j;
-        if (!mbar_wait(&s.v_empty[st], ph ^ 1, abort, p.status, TC_SITE(1, 2, j))) break;
-        mbar_arrive_expect_tx(&s.v_full[st], kTileBytes);
-        tma_load_4d(s.v[st], &map_v, &s.v_full[st], 0, head, j * kBN, b);
-        last_v = j;
+      uint32_t c = 0;  // K/V ring position over all units of this CTA
+      int n_units = 0;
+      int last_k = -1, last_v = -1;  // ring positions of the last tiles issued, for the wind-down
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x) {
+        const Unit w = unit_of(p, u);
+        if (w.nkv == 0) continue;  // (every role skips such a unit alike)
+        // The Q buffer is free once the previous unit's last S has run.
+        if (n_units > 0 &&
+            !mbar_wait(&s.q_empty, (n_units - 1) & 1, abort, p.status, TC_SITE(1, 0, n_units)))
+          break;
+        mbar_arrive_expect_tx(&s.q_full, w.n_tiles * kTileBytes);
+        for (int t = 0; t < w.n_tiles; ++t)
+          tma_load_4d(s.q[t], &map_q, &s.q_full, 0, w.head, w.q0 + t * kBM, w.b);
+        for (int j = 0; j < w.nkv; ++j, ++c) {
+          const int st = c % kStages;
+          const uint32_t ph = (c / kStages) & 1;
+          if (!mbar_wait(&s.k_empty[st], ph ^ 1, abort, p.status, TC_SITE(1, 1, j))) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&s.k_full[st], kTileBytes);
+          tma_load_4d(s.k[st], &map_k, &s.k_full[st], 0, w.head, j * kBN, w.b);
+          last_k = (int)c;
+          if (!mbar_wait(&s.v_empty[st], ph ^ 1, abort, p.status, TC_SITE(1, 2, j))) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&s.v_full[st], kTileBytes);
+          tma_load_4d(s.v[st], &map_v, &s.v_full[st], 0, w.head, j * kBN, w.b);
+          last_v = (int)c;
+        }
+        ++n_units;
       }
       if (*abort) {
         // Wind-down after a timeout: let the loads still in flight land
@@ -181,7 +229,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == kMmaWarp) {
     // ---------------------------------------------------------- MMA issuer
-    if (lane == 0 && nkv > 0) {
+    if (lane == 0) {
       constexpr uint32_t ab = IN_DT == WATTN_BF16 ? 1u : 0u;
       constexpr uint32_t idesc_s = idesc_f16(ab, kBM, kBN, 0, 0);  // Q, K both K-major
       constexpr uint32_t idesc_o = idesc_f16(ab, kBM, 64, 0, 1);   // P from TMEM, V MN-major
@@ -204,51 +252,75 @@ __global__ void __launch_bounds__(kThreads, 1)
                   smem_desc_sw128(va + kk * 2048, 16384, 1024), idesc_o, acc || kk > 0);
       };
 
-      bool ok = mbar_wait(&s.q_full, 0, abort, p.status, TC_SITE(2, 0, 0)) &&
-                mbar_wait(&s.k_full[0], 0, abort, p.status, TC_SITE(2, 1, 0));
-      if (ok) {
-        tc_fence_after();
-        for (int t = 0; t < n_tiles; ++t) {
-          issue_s(t, 0);
+      // Running counts per tile (barrier phases continue across units).
+      uint32_t n_s[kTiles] = {0, 0}, n_pv[kTiles] = {0, 0}, n_ep[kTiles] = {0, 0};
+      uint32_t c = 0;  // K/V ring position
+      int n_units = 0;
+      bool ok = true;
+      // S(t) for key tile at ring position cs: waits until the softmax has
+      // taken the previous S of tile t into registers.
+      auto s_step = [&](const Unit &w, uint32_t cs, int j) -> bool {
+        const int st = cs % kStages;
+        if (!mbar_wait(&s.k_full[st], (cs / kStages) & 1, abort, p.status, TC_SITE(2, 5, j)))
+          return false;
+        for (int t = 0; t < w.n_tiles; ++t) {
+          if (n_s[t] > 0 &&
+              !mbar_wait(&s.s_free[t], (n_s[t] - 1) & 1, abort, p.status, TC_SITE(2, 7 + t, j)))
+            return false;
+          tc_fence_after();
+          issue_s(t, st);
           umma_commit(&s.s_full[t]);
+          ++n_s[t];
         }
-        umma_commit(&s.k_empty[0]);
-      }
-      // Per key tile j: first S(t, j+1) for both tiles, as soon as the
-      // softmax has taken S(t, j) into registers (s_free), so the next
-      // scores are computed while the softmax works on this tile; then
-      // PV(t, j) once P(t, j) is in TMEM (p_full).
-      for (int j = 0; ok && j < nkv; ++j) {
-        const int st = j % kStages;
-        const uint32_t ph = (j / kStages) & 1;
-        const int jn = j + 1, stn = jn % kStages;
-        const uint32_t phn = (jn / kStages) & 1;
-        if (jn < nkv) {
-          if (!mbar_wait(&s.k_full[stn], phn, abort, p.status, TC_SITE(2, 5, jn))) break;
-          for (int t = 0; t < n_tiles; ++t) {
-            if (!mbar_wait(&s.s_free[t], j & 1, abort, p.status, TC_SITE(2, 7 + t, j))) {
+        umma_commit(&s.k_empty[st]);
+        return true;
+      };
+      for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x) {
+        const Unit w = unit_of(p, u);
+        if (w.nkv == 0) continue;
+        if (!mbar_wait(&s.q_full, n_units & 1, abort, p.status, TC_SITE(2, 0, n_units))) break;
+        if (!s_step(w, c, 0)) break;
+        // Per key tile j: first S(t, j+1), as soon as the softmax has taken
+        // S(t, j) into registers, so the next scores are computed while the
+        // softmax works on this tile; then PV(t, j) once P(t, j) is in TMEM.
+        for (int j = 0; j < w.nkv; ++j) {
+          const uint32_t cj = c + j;
+          const int st = cj % kStages;
+          if (j + 1 < w.nkv) {
+            if (!s_step(w, cj + 1, j + 1)) {
+              ok = false;
+              break;
+            }
+          } else {
+            umma_commit(&s.q_empty);  // the unit's last S: Q may be replaced
+          }
+          if (!mbar_wait(&s.v_full[st], (cj / kStages) & 1, abort, p.status, TC_SITE(2, 2, j))) {
+            ok = false;
+            break;
+          }
+          for (int t = 0; t < w.n_tiles; ++t) {
+            // The unit's first PV overwrites O(t): the previous unit's
+            // epilogue must have read it.
+            if (j == 0 && n_ep[t] > 0 &&
+                !mbar_wait(&s.o_free[t], (n_ep[t] - 1) & 1, abort, p.status, TC_SITE(2, 9, j))) {
+              ok = false;
+              break;
+            }
+            if (!mbar_wait(&s.p_full[t], n_pv[t] & 1, abort, p.status, TC_SITE(2, 3 + t, j))) {
               ok = false;
               break;
             }
             tc_fence_after();
-            issue_s(t, stn);
-            umma_commit(&s.s_full[t]);
+            issue_pv(t, st, j > 0);
+            umma_commit(&s.o_done[t]);
+            ++n_pv[t];
           }
           if (!ok) break;
-          umma_commit(&s.k_empty[stn]);
+          umma_commit(&s.v_empty[st]);
         }
-        if (!mbar_wait(&s.v_full[st], ph, abort, p.status, TC_SITE(2, 2, j))) break;
-        for (int t = 0; t < n_tiles; ++t) {
-          if (!mbar_wait(&s.p_full[t], j & 1, abort, p.status, TC_SITE(2, 3 + t, j))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          issue_pv(t, st, j > 0);
-          umma_commit(&s.o_done[t]);
-        }
-        if (!ok) break;
-        umma_commit(&s.v_empty[st]);
+        for (int t = 0; t < w.n_tiles; ++t) ++n_ep[t];
+        c += w.nkv;
+        ++n_units;
       }
       // Drain: every MMA issued above completes before TMEM is freed. This
       // wait ignores `abort` (it must outlive a wind-down) but stays bounded.
@@ -261,17 +333,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int t = warp >> 2;   // query tile of this warpgroup
     const int wq = warp & 3;   // TMEM lane quarter of this warp
     const int row = wq * 32 + lane;
-    if (t < n_tiles && nkv > 0) {
-      const uint32_t lane_base = tmem + (uint32_t(wq * 32) << 16);
-      const uint32_t t_s = lane_base + t * 256;
-      const uint32_t t_p = t_s + 128, t_o = t_s + 192;
-      const int qrow = q0 + t * kBM + row;
+    const uint32_t lane_base = tmem + (uint32_t(wq * 32) << 16);
+    const uint32_t t_s = lane_base + t * 256;
+    const uint32_t t_p = t_s + 128, t_o = t_s + 192;
+    const float c = p.scale_log2;
+    uint32_t n_s = 0, n_p = 0;  // S tiles read and P tiles written by this warpgroup
+    bool ok = true;
+    for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x) {
+      const Unit w = unit_of(p, u);
+      if (w.nkv == 0 || t >= w.n_tiles) continue;
+      const int qrow = w.q0 + t * kBM + row;
       const int key_lim = p.causal ? min(p.t_kv, qrow + p.q_pos_offset + 1) : p.t_kv;
-      const float c = p.scale_log2;
       float m = -INFINITY, l = 0.f;
-      bool ok = true;
-      for (int j = 0; j < nkv; ++j) {
-        const bool got = mbar_wait(&s.s_full[t], j & 1, abort, p.status, TC_SITE(3 + t, 0, j));
+      for (int j = 0; j < w.nkv; ++j, ++n_s) {
+        const bool got =
+            mbar_wait(&s.s_full[t], n_s & 1, abort, p.status, TC_SITE(3 + t, 0, j));
         // The whole warp takes the same branch and is converged before the
         // .sync.aligned TMEM accesses below.
         if (!__all_sync(0xffffffffu, got)) {
@@ -285,7 +361,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld();
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) reg_fence(r[q4]);
-        // S(t, j) is in registers: the MMA warp may compute S(t, j+1) now.
+        // S(t, j) is in registers: the MMA warp may compute the next S now.
         tc_fence_before();
         mbar_arrive(&s.s_free[t]);
         float sv[128];
@@ -324,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float mu = (m == -INFINITY) ? 0.f : m;
         const float2 c2 = make_float2(c, c), nmu2 = make_float2(-mu, -mu);
         // P = 2^(s*c - mu), packed to 16-bit pairs (kept in registers until
-        // PV(t, j-1) is done, then stored to TMEM). l sums the *rounded*
+        // the previous PV is done, then stored to TMEM). l sums the *rounded*
         // weights the tensor core multiplies V with: they then sum to
         // exactly one and the rounding error of a dominant weight cancels
         // in acc / l.
@@ -335,23 +411,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 64; ++i) {
           const float2 x = __ffma2_rn(make_float2(sv[2 * i], sv[2 * i + 1]), c2, nmu2);
           float2 pv;
-          if (kFmaExp2Every > 0 && i % kFmaExp2Every == kFmaExp2Every - 1) {
+          if (fma_exp2_slot(i)) {
             pv = exp2_fma2(x);
           } else {
             pv.x = ex2(x.x);
             pv.y = ex2(x.y);
           }
-          const uint32_t w = pack2<InT>(pv.x, pv.y);
-          pk[i] = w;
-          acc2[i & 3] = __fadd2_rn(acc2[i & 3], unpack2<InT>(w));
+          const uint32_t wd = pack2<InT>(pv.x, pv.y);
+          pk[i] = wd;
+          acc2[i & 3] = __fadd2_rn(acc2[i & 3], unpack2<InT>(wd));
         }
         l += (acc2[0].x + acc2[0].y) + (acc2[1].x + acc2[1].y) + (acc2[2].x + acc2[2].y) +
              (acc2[3].x + acc2[3].y);
-        // P(t, j) may only overwrite P(t, j-1) once PV(t, j-1) has read it,
-        // and O may only be rescaled once PV(t, j-1) has added to it.
-        if (j > 0) {
+        // P may only overwrite the previous P once the PV reading it is
+        // done (also across units), and O may only be rescaled once the
+        // previous PV of this unit has added to it.
+        if (n_p > 0) {
           const bool done =
-              mbar_wait(&s.o_done[t], (j - 1) & 1, abort, p.status, TC_SITE(3 + t, 2, j));
+              mbar_wait(&s.o_done[t], (n_p - 1) & 1, abort, p.status, TC_SITE(3 + t, 2, j));
           if (!__all_sync(0xffffffffu, done)) {
             ok = false;
             break;
@@ -386,23 +463,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&s.p_full[t]);
+        ++n_p;
       }
-      const bool fin =
-          ok && mbar_wait(&s.o_done[t], (nkv - 1) & 1, abort, p.status, TC_SITE(3 + t, 1, nkv));
-      if (__all_sync(0xffffffffu, fin)) {
-        tc_fence_after();
-        uint32_t o[2][32];
-        tmem_ld32(t_o, o[0]);
-        tmem_ld32(t_o + 32, o[1]);
-        tmem_wait_ld();
-        reg_fence(o[0]);
-        reg_fence(o[1]);
-        if (qrow < p.t_q) {
-          const float inv = l > 0.f ? 1.f / l : 0.f;
-          OutT *dst = reinterpret_cast<OutT *>(p.o) + (int64_t)b * p.o_bs +
-                      (int64_t)qrow * p.o_rs + head * kHeadDim;
-          store_row<OutT>(dst, o, inv);
-        }
+      if (!ok) break;
+      // ---- epilogue: O(t) / l; the tile's O columns are then free for the
+      // next unit's first PV.
+      const bool fin = mbar_wait(&s.o_done[t], (n_p - 1) & 1, abort, p.status,
+                                 TC_SITE(3 + t, 1, w.nkv));
+      if (!__all_sync(0xffffffffu, fin)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t o[2][32];
+      tmem_ld32(t_o, o[0]);
+      tmem_ld32(t_o + 32, o[1]);
+      tmem_wait_ld();
+      reg_fence(o[0]);
+      reg_fence(o[1]);
+      tc_fence_before();
+      mbar_arrive(&s.o_free[t]);
+      if (qrow < p.t_q) {
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        OutT *dst = reinterpret_cast<OutT *>(p.o) + (int64_t)w.b * p.o_bs +
+                    (int64_t)qrow * p.o_rs + w.head * kHeadDim;
+        store_row<OutT>(dst, o, inv);
       }
     }
   }
@@ -426,7 +511,13 @@ int launch_typed(const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
       cudaSuccess)
     return check_launch("cudaFuncSetAttribute(attn_fwd_tc)");
-  dim3 grid((p.t_q + kBM * kTiles - 1) / (kBM * kTiles), n_heads, batch);
+  // Persistent grid: one CTA per SM (the shared memory allows no second),
+  // each walking units blockIdx.x, blockIdx.x + gridDim.x, ...
+  int dev = 0, n_sm = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return check_launch("attn_fwd_tc: device query");
+  dim3 grid(std::min(p.n_units, n_sm));
   kern<<<grid, kThreads, smem, stream>>>(mq, mk, mv, p);
   return check_launch("attn_fwd_tc");
 }
@@ -462,6 +553,12 @@ int launch_attn_tc(const void *q, const void *k, const void *v, void *o, int in_
   p.scale_log2 = scale * 1.4426950408889634f;
   p.causal = causal;
   p.q_pos_offset = q_pos_offset;
+  p.n_qblk = (t_q + kBM * kTiles - 1) / (kBM * kTiles);
+  p.n_heads = n_heads;
+  const long long n_units = (long long)p.n_qblk * n_heads * batch;
+  if (n_units > INT_MAX)
+    return set_error(WATTN_ERR_INVALID, "attention: %lld work units exceed 2^31", n_units);
+  p.n_units = (int)n_units;
   p.status = device_status_ptr();
   if (p.status == nullptr) return WATTN_ERR_CUDA;
   if (in_dtype == WATTN_F16) {

@@ -38,8 +38,11 @@ WATTN_DEVINL unsigned long long globaltimer_ns() {
 
 // status[0]: status word; status[1]: site of the first wait that ran out
 // (kernel << 24 | role << 16 | barrier << 8 | iteration & 0xff).
+WATTN_DEVINL void report_error(int *status, int code, int site) {
+  if (atomicCAS(status, WATTN_OK, code) == WATTN_OK) atomicExch(status + 1, site);
+}
 WATTN_DEVINL void report_timeout(int *status, int site) {
-  if (atomicCAS(status, WATTN_OK, WATTN_ERR_TIMEOUT) == WATTN_OK) atomicExch(status + 1, site);
+  report_error(status, WATTN_ERR_TIMEOUT, site);
 }
 
 // ------------------------------------------------------------ element types
