@@ -565,16 +565,17 @@ def main():
         line["decode"] = {"config": "c5_turbo_self_paged_plus_cross", "value": dec["value"],
                           "unit": "GB/s", "frac_of_hbm": dec["value"] / peaks["hbm_gbs"],
                           "ms": dec["ms"], "launches": dec["launches"],
-                          "mean_cache_len": dec["mean_cache_len"]}
+                          "mean_cache_len": dec["mean_cache_len"],
+                          "paged_kernel_traffic": load_traffic().get("decode_stream_paged_c5_layer")}
     if xdec:
         line["cross_decode"] = {"config": "c4_large_v3_cross", "value": xdec["value"],
                                 "unit": "GB/s",
-                                "roofline": {"bound": "hbm", "kernel": "decode_dense",
+                                "roofline": {"bound": "hbm", "kernel": "decode_stream_dense",
                                              "achieved": xdec["achieved"], "peak": peaks["hbm_gbs"],
                                              "unit": "GB/s",
                                              "frac": xdec["achieved"] / peaks["hbm_gbs"],
                                              "bytes_per_launch": xdec["bytes_per_launch"],
-                                             "traffic": load_traffic().get("decode_dense_c4_layer")},
+                                             "traffic": load_traffic().get("decode_stream_dense_c4_layer")},
                                 "ms": xdec["ms"], "launches": xdec["launches"]}
     if also:
         line["also"] = also

@@ -142,6 +142,31 @@ def test_ragged_batch_many_rows(W, oracle, dtype):
     h.step(slots[::3], [int(x) for x in rng.integers(1, 12, size=len(slots[::3]))])
 
 
+@pytest.mark.parametrize("src, dst, pad", [(1, 1, 3), (0, 2, 0), (2, 2, 8)],
+                         ids=["f16_unaligned_rows", "f32_to_bf16", "bf16_padded_rows"])
+def test_append_row_layouts(W, src, dst, pad):
+    """Rows appended from strided sources (row stride = width + pad, so some
+    are not 16-byte aligned and take the element-wise path) and with a type
+    conversion land bit-exact in the pages."""
+    import torch
+    tdt = {0: torch.float32, 1: torch.float16, 2: torch.bfloat16}
+    H, n = 4, 37
+    d = H * 64
+    c = W.DeviceKvCache(1, 2, H, 128, page_rows=64, dtype=dst)
+    g = torch.Generator(device="cuda").manual_seed(3)
+    base_k = torch.randn(n, d + pad, generator=g, device="cuda").to(tdt[src])
+    base_v = torch.randn(n, d + pad, generator=g, device="cuda").to(tdt[src])
+    k, v = base_k[:, :d], base_v[:, :d]       # row stride d + pad
+    c.append(0, [1], [n], k, v)
+    c.advance([1], [n])
+    for which, ref in ((0, k), (1, v)):
+        out = torch.empty(n, d, dtype=tdt[dst], device="cuda")
+        c.read_slot(0, 1, which, out)
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref.to(tdt[dst])), which
+    c.close()
+
+
 def test_cache_errors(W):
     c = W.DeviceKvCache(1, 2, 2, 128)
     with pytest.raises(W.WattnError) as e:

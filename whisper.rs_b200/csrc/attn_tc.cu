@@ -43,7 +43,7 @@ namespace {
 constexpr int kBM = 128;                 // query rows per tile (UMMA M)
 constexpr int kBN = 128;                 // keys per tile
 constexpr int kTiles = 2;                // query tiles per CTA
-constexpr int kStages = 3;               // K/V ring depth
+constexpr int kStages = 4;               // K/V ring depth
 constexpr int kTileBytes = 128 * 128;    // 128 rows x 64 x 16-bit
 constexpr int kTmaWarp = 4 * kTiles;     // warp 8
 constexpr int kMmaWarp = kTmaWarp + 1;   // warp 9

@@ -278,15 +278,18 @@ WATTN_DEVINL DecWork dec_item(const DecParams &p, const PagedTable *pt, int it) 
 WATTN_DEVINL void compute_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 // Issues the TMA loads of the K and V sub-tiles that start at key `key`,
-// each completing on its own barrier.
+// each completing on its own barrier. Dense: map_k / map_v are the K and V
+// tensors. Paged: both view the page pool, map_k with 64-row boxes and
+// map_v with kDecTailRows-row boxes; a sub-tile of which only `rows` < 64
+// keys are attended loads just the 16-row boxes covering them (the rows
+// left unloaded keep finite data of earlier sub-tiles or the initial zeros
+// and are masked).
 template <int KV_DT, bool PAGED>
 WATTN_DEVINL void issue_sub(uint8_t *kdst, uint8_t *vdst, uint64_t *kbar, uint64_t *vbar,
                             const CUtensorMap &map_k, const CUtensorMap &map_v,
                             const DecParams &p, const PagedTable *pt, const DecRows &rw,
-                            int head, int key) {
+                            int head, int key, int rows) {
   using G = KvGeom<KV_DT>;
-  mbar_arrive_expect_tx(kbar, G::sub_bytes);
-  mbar_arrive_expect_tx(vbar, G::sub_bytes);
   if constexpr (PAGED) {
     // Pool rows: (((page * n_layers + layer) * 2 + kv) * n_heads + head) * page_rows + r
     const int page = pt->pages[rw.entry][key / pt->page_rows];
@@ -295,12 +298,33 @@ WATTN_DEVINL void issue_sub(uint8_t *kdst, uint8_t *vdst, uint64_t *kbar, uint64
         ((((int64_t)page * pt->n_layers + pt->layer) * 2 + 0) * p.n_heads + head) *
             pt->page_rows + r_in;
     const int64_t rv = rk + (int64_t)p.n_heads * pt->page_rows;
+    if (rows >= kDecSub) {
+      mbar_arrive_expect_tx(kbar, G::sub_bytes);
+      mbar_arrive_expect_tx(vbar, G::sub_bytes);
 #pragma unroll
-    for (int bk = 0; bk < G::blocks; ++bk) {
-      tma_load_2d(kdst + bk * kDecSub * 128, &map_k, kbar, bk * G::block_elems, (int)rk);
-      tma_load_2d(vdst + bk * kDecSub * 128, &map_v, vbar, bk * G::block_elems, (int)rv);
+      for (int bk = 0; bk < G::blocks; ++bk) {
+        tma_load_2d(kdst + bk * kDecSub * 128, &map_k, kbar, bk * G::block_elems, (int)rk);
+        tma_load_2d(vdst + bk * kDecSub * 128, &map_k, vbar, bk * G::block_elems, (int)rv);
+      }
+    } else {
+      const int n_box = (rows + kDecTailRows - 1) / kDecTailRows;
+      const uint32_t bytes = n_box * kDecTailRows * 128 * G::blocks;
+      mbar_arrive_expect_tx(kbar, bytes);
+      mbar_arrive_expect_tx(vbar, bytes);
+      for (int i = 0; i < n_box; ++i) {
+        const int off = i * kDecTailRows;
+#pragma unroll
+        for (int bk = 0; bk < G::blocks; ++bk) {
+          tma_load_2d(kdst + bk * kDecSub * 128 + off * 128, &map_v, kbar, bk * G::block_elems,
+                      (int)(rk + off));
+          tma_load_2d(vdst + bk * kDecSub * 128 + off * 128, &map_v, vbar, bk * G::block_elems,
+                      (int)(rv + off));
+        }
+      }
     }
   } else {
+    mbar_arrive_expect_tx(kbar, G::sub_bytes);
+    mbar_arrive_expect_tx(vbar, G::sub_bytes);
 #pragma unroll
     for (int bk = 0; bk < G::blocks; ++bk) {
       tma_load_4d(kdst + bk * kDecSub * 128, &map_k, kbar, bk * G::block_elems, head, key,
@@ -403,6 +427,13 @@ __device__ void decode_stream_body(const CUtensorMap &map_k, const CUtensorMap &
       (reinterpret_cast<uintptr_t>(dec_smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
+  if constexpr (PAGED) {
+    // Tail sub-tiles load only their attended rows: the V rows they leave
+    // must hold finite values (they meet p = 0), so the ring starts zeroed.
+    uint4 *v4 = reinterpret_cast<uint4 *>(&s.v[0][0]);
+    for (int i = tid; i < (int)(sizeof(s.v) / 16); i += blockDim.x) v4[i] = make_uint4(0, 0, 0, 0);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
   if (tid == 0) {
     for (int st = 0; st < kStrStages; ++st) {
       mbar_init(&s.kfull[st], 1);
@@ -427,8 +458,9 @@ __device__ void decode_stream_body(const CUtensorMap &map_k, const CUtensorMap &
           if (!mbar_wait(&s.empty[stage], ph ^ 1, abort, p.status,
                          (2 << 24) | (3 << 16) | ((c & 0xff) << 8)))
             return;
+          const int key = w.k_beg + st * kDecSub;
           issue_sub<DT, PAGED>(s.k[stage], s.v[stage], &s.kfull[stage], &s.vfull[stage], map_k,
-                               map_v, p, pt, w.rw, w.head, w.k_beg + st * kDecSub);
+                               map_v, p, pt, w.rw, w.head, key, w.rw.kv_hi - key);
         }
       }
     }
@@ -586,7 +618,7 @@ __device__ void decode_simt_body(const CUtensorMap &map_k, const CUtensorMap &ma
     fence_barrier_init();
     for (int st = 0; st < n_sub; ++st)
       issue_sub<KV_DT, PAGED>(s.k[st], s.v[st], &s.kbar[st], &s.vbar[st], map_k, map_v, p, pt,
-                              rw, head, k_beg + st * kDecSub);
+                              rw, head, k_beg + st * kDecSub, kDecSub);
   }
 
   // Query rows, pre-scaled into the exp2 domain.

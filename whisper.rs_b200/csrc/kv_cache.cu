@@ -40,8 +40,42 @@ struct AppendTable {
   int row_in_page[kAppendMaxRows];
 };
 
+// Eight consecutive elements through f32 (exact for every type pair the
+// cache stores: a 16-bit value round-trips through f32 unchanged).
+template <typename T>
+WATTN_DEVINL void load8(const T *src, float (&f)[8]) {
+  if constexpr (sizeof(T) == 4) {
+    const float4 a = reinterpret_cast<const float4 *>(src)[0];
+    const float4 b = reinterpret_cast<const float4 *>(src)[1];
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  } else {
+    const uint4 w = *reinterpret_cast<const uint4 *>(src);
+    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 x = unpack2<T>(u[i]);
+      f[2 * i] = x.x;
+      f[2 * i + 1] = x.y;
+    }
+  }
+}
+
+template <typename T>
+WATTN_DEVINL void store8(T *dst, const float (&f)[8]) {
+  if constexpr (sizeof(T) == 4) {
+    reinterpret_cast<float4 *>(dst)[0] = make_float4(f[0], f[1], f[2], f[3]);
+    reinterpret_cast<float4 *>(dst)[1] = make_float4(f[4], f[5], f[6], f[7]);
+  } else {
+    *reinterpret_cast<uint4 *>(dst) = make_uint4(pack2<T>(f[0], f[1]), pack2<T>(f[2], f[3]),
+                                                 pack2<T>(f[4], f[5]), pack2<T>(f[6], f[7]));
+  }
+}
+
 // Scatter new K/V rows ([n_rows][n_heads*64], src type) into their pages.
-template <typename SrcT, typename DstT>
+// VEC: source rows 16-byte aligned, so each thread moves 8 elements with
+// vector loads and stores (page rows always are: 64 elements per head).
+template <typename SrcT, typename DstT, bool VEC>
 __global__ void kv_append_kernel(const SrcT *k_rows, const SrcT *v_rows, DstT *pool,
                                  const __grid_constant__ AppendTable t) {
   const int r = blockIdx.x;
@@ -50,11 +84,23 @@ __global__ void kv_append_kernel(const SrcT *k_rows, const SrcT *v_rows, DstT *p
   DstT *layer_base = pool + (int64_t)t.page[r] * page_elems +
                      (int64_t)t.layer * 2 * t.n_heads * t.page_rows * 64;
   const int64_t kv_off = (int64_t)t.n_heads * t.page_rows * 64;
-  for (int i = threadIdx.x; i < width; i += blockDim.x) {
-    const int h = i >> 6, d = i & 63;
-    const int64_t dst = ((int64_t)h * t.page_rows + t.row_in_page[r]) * 64 + d;
-    layer_base[dst] = from_f32<DstT>(to_f32(k_rows[(int64_t)r * t.row_stride + i]));
-    layer_base[kv_off + dst] = from_f32<DstT>(to_f32(v_rows[(int64_t)r * t.row_stride + i]));
+  if constexpr (VEC) {
+    for (int i = threadIdx.x * 8; i < width; i += blockDim.x * 8) {
+      const int h = i >> 6, d = i & 63;
+      const int64_t dst = ((int64_t)h * t.page_rows + t.row_in_page[r]) * 64 + d;
+      float f[8];
+      load8<SrcT>(k_rows + (int64_t)r * t.row_stride + i, f);
+      store8<DstT>(layer_base + dst, f);
+      load8<SrcT>(v_rows + (int64_t)r * t.row_stride + i, f);
+      store8<DstT>(layer_base + kv_off + dst, f);
+    }
+  } else {
+    for (int i = threadIdx.x; i < width; i += blockDim.x) {
+      const int h = i >> 6, d = i & 63;
+      const int64_t dst = ((int64_t)h * t.page_rows + t.row_in_page[r]) * 64 + d;
+      layer_base[dst] = from_f32<DstT>(to_f32(k_rows[(int64_t)r * t.row_stride + i]));
+      layer_base[kv_off + dst] = from_f32<DstT>(to_f32(v_rows[(int64_t)r * t.row_stride + i]));
+    }
   }
 }
 
@@ -80,17 +126,28 @@ __global__ void kv_gather_kernel(const SrcT *pool, DstT *out, const __grid_const
   }
 }
 
+template <typename SrcT, bool VEC>
+void launch_append_vec(int dst_dt, const SrcT *ks, const SrcT *vs, void *pool,
+                       const AppendTable &t, cudaStream_t st) {
+  const dim3 grid(t.n_rows);
+  const int threads = VEC ? 160 : 256;  // VEC: 160 x 8 = the 1280 elements of a large-v3 row
+  if (dst_dt == WATTN_F32)
+    kv_append_kernel<SrcT, float, VEC><<<grid, threads, 0, st>>>(ks, vs, (float *)pool, t);
+  else if (dst_dt == WATTN_F16)
+    kv_append_kernel<SrcT, __half, VEC><<<grid, threads, 0, st>>>(ks, vs, (__half *)pool, t);
+  else
+    kv_append_kernel<SrcT, __nv_bfloat16, VEC>
+        <<<grid, threads, 0, st>>>(ks, vs, (__nv_bfloat16 *)pool, t);
+}
+
 template <typename SrcT>
 int launch_append_src(int dst_dt, const void *k, const void *v, void *pool, const AppendTable &t,
                       cudaStream_t st) {
-  dim3 grid(t.n_rows);
   const SrcT *ks = (const SrcT *)k, *vs = (const SrcT *)v;
-  if (dst_dt == WATTN_F32)
-    kv_append_kernel<SrcT, float><<<grid, 256, 0, st>>>(ks, vs, (float *)pool, t);
-  else if (dst_dt == WATTN_F16)
-    kv_append_kernel<SrcT, __half><<<grid, 256, 0, st>>>(ks, vs, (__half *)pool, t);
-  else
-    kv_append_kernel<SrcT, __nv_bfloat16><<<grid, 256, 0, st>>>(ks, vs, (__nv_bfloat16 *)pool, t);
+  const bool vec = ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15) == 0 &&
+                   (t.row_stride * (int64_t)sizeof(SrcT)) % 16 == 0;
+  if (vec) launch_append_vec<SrcT, true>(dst_dt, ks, vs, pool, t, st);
+  else launch_append_vec<SrcT, false>(dst_dt, ks, vs, pool, t, st);
   return check_launch("kv_append");
 }
 
@@ -125,7 +182,8 @@ struct wattn_kv_cache {
   int max_pages_per_slot = 0;
   size_t page_bytes = 0;
   uint8_t *pool = nullptr;
-  CUtensorMap map;
+  CUtensorMap map;       // the pool as [rows][64], boxes of kDecSubRows rows
+  CUtensorMap map_tail;  // the same, boxes of kDecTailRows rows
   std::vector<int> refcnt;
   std::vector<int> free_pages;
   std::vector<Slot> slots;
@@ -216,8 +274,12 @@ int wattn_kv_create(wattn_kv_cache **out, int n_layers, int n_slots, int n_heads
   const uint64_t dims[2] = {64, total_rows};
   const uint64_t strides[1] = {64ull * es};
   const uint32_t box[2] = {(uint32_t)(128 / es), (uint32_t)kDecSubRows};
+  const uint32_t box_tail[2] = {(uint32_t)(128 / es), (uint32_t)kDecTailRows};
   int rc = encode_tmap(&c->map, tmap_dtype(dtype), 2, c->pool, dims, strides, box,
                        CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc == WATTN_OK)
+    rc = encode_tmap(&c->map_tail, tmap_dtype(dtype), 2, c->pool, dims, strides, box_tail,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != WATTN_OK) {
     cudaFree(c->pool);
     delete c;
@@ -543,7 +605,7 @@ int wattn_kv_attend(wattn_kv_cache *c, int layer, const int *slots, const int *n
       sorted.kv_hi[e] = pt.kv_hi[r];
       for (int pi = 0; pi < kPagedMaxPages; ++pi) sorted.pages[e][pi] = pt.pages[r][pi];
     }
-    int rc = launch_decode_paged(c->map, c->map, qp, op, q_dtype, c->dtype, out_dtype, c->n_heads,
+    int rc = launch_decode_paged(c->map, c->map_tail, qp, op, q_dtype, c->dtype, out_dtype, c->n_heads,
                                  q_row_stride, o_row_stride, scale, sorted, max_keys, workspace,
                                  workspace_bytes, st);
     row_base += pt.n_rows;

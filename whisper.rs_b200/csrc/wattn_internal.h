@@ -72,6 +72,7 @@ int launch_decode(const void *q, const void *k, const void *v, void *o, int q_dt
 
 // ----------------------------------------------------------- paged decode
 constexpr int kDecSubRows = 64;     // keys per decode sub-tile (TMA box rows)
+constexpr int kDecTailRows = 16;    // box rows of the paged tail loads
 constexpr int kPagedMaxRows = 384;  // query rows per paged launch
 constexpr int kPagedMaxPages = 16;  // pages per row in one launch
 
@@ -90,7 +91,9 @@ struct PagedTable {
   int pages[kPagedMaxRows][kPagedMaxPages];
 };
 
-// `map_k` / `map_v` view the page pool as 2-D [rows][64] (box 64 rows).
+// `map_k` / `map_v` view the page pool as 2-D [rows][64], map_k with boxes
+// of kDecSubRows rows and map_v with boxes of kDecTailRows rows (for the
+// last, partly attended sub-tile of a row's keys).
 int launch_decode_paged(const CUtensorMap &map_k, const CUtensorMap &map_v, const void *q,
                         void *o, int q_dtype, int kv_dtype, int out_dtype, int n_heads,
                         int64_t q_rs, int64_t o_rs, float scale, const PagedTable &pt,
