@@ -563,7 +563,7 @@ def main():
     }
     if dec:
         line["decode"] = {"config": "c5_turbo_self_paged_plus_cross", "value": dec["value"],
-                          "unit": "GB/s", "frac_of_hbm": dec["value"] / peaks["hbm_gbs"],
+                          "unit": "GB/s", "frac_of_hbm": dec["value"] / (peaks["hbm_gbs"] * world),
                           "ms": dec["ms"], "launches": dec["launches"],
                           "mean_cache_len": dec["mean_cache_len"],
                           "paged_kernel_traffic": load_traffic().get("decode_stream_paged_c5_layer")}

@@ -45,6 +45,22 @@ def test_decode_dense(W, oracle, kv_dt, t_kv, g):
         check_16bit(out, ref, f"dt={kv_dt} t_kv={t_kv} g={g}")
 
 
+@pytest.mark.parametrize("kv_dt", [1, 2], ids=["f16", "bf16"])
+@pytest.mark.parametrize("t_kv", [4000, 4033])
+def test_decode_many_splits(W, oracle, kv_dt, t_kv):
+    # One utterance, one head: few items, so the keys are split (16 splits of
+    # 256 keys here) and merged by log-sum-exp; the second length leaves a
+    # ragged last split.
+    n_groups, g, h = 1, 5, 1
+    d = h * 64
+    (kd, kf), (vd, vf) = rounded(randn(40 + t_kv, t_kv * d), kv_dt), \
+        rounded(randn(41 + t_kv, t_kv * d), kv_dt)
+    qd, qf = rounded(randn(42, g * d), kv_dt)
+    ref = oracle.decode_grouped(qf, kf, vf, n_groups, g, t_kv, h, d)
+    out = _decode(W, qd, kd, vd, 0, n_groups, g, t_kv, h)
+    check_16bit(out, ref, f"dt={kv_dt} t_kv={t_kv}")
+
+
 def test_decode_cross_attention_large_v3(W, oracle):
     # Config 4 at full size, one layer: 32 utterances x 5 beams, 20 heads,
     # f16 K/V of 1500 encoder states shared by the beams of an utterance.

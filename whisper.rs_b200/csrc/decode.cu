@@ -46,6 +46,10 @@ constexpr int kStrStages = 4;      // tensor-core path: depth of the K/V ring (s
 constexpr int kStrWarps = 4;       // compute warps; one more warp issues the loads
 constexpr int kStrThreads = (kStrWarps + 1) * 32;
 constexpr int kStrSlots = 148 * 3; // resident tensor-core CTAs on a B200: three per SM
+// Splits are made only while the items number below this (measured on B200:
+// a split costs a partial write, a fence and an atomic per item, ~5 us, so
+// it pays only when a handful of items would leave most SMs idle).
+constexpr int kStrSplitTarget = 160;
 constexpr int kStrMinSubs = 4;     // sub-tiles per split below which no further split is made
 constexpr bool kStrPagedPersist = true;  // paged entries come sorted by length
 // Workspace layout, the same for every call: [counters][partials]. The
@@ -376,19 +380,47 @@ __device__ void finish_split(const DecParams &p, const float *red, const float *
   }
   if constexpr (NAMED) compute_sync(); else __syncthreads();
   if (!*s_last) return;
-  for (int i = tid; i < rw.nr * 64; i += nt) {
-    const int r = i >> 6, d = i & 63;
+  // One warp per row, two dims per lane; the splits' partials are read four
+  // at a time with independent loads (they sit in L2).
+  const int n_warps = nt >> 5, wid = tid >> 5, ln = tid & 31;
+  for (int r = wid; r < rw.nr; r += n_warps) {
     const float *part0 =
         p.part + ((part_base + (int64_t)r * p.n_heads + head) * p.n_splits) * kPartStride;
     float M = -INFINITY;
-    for (int sp = 0; sp < n_splits; ++sp) M = fmaxf(M, __ldcg(part0 + sp * kPartStride + 64));
-    float L = 0.f, O = 0.f;
-    for (int sp = 0; sp < n_splits; ++sp) {
-      const float w = ex2(__ldcg(part0 + sp * kPartStride + 64) - M);
-      L = fmaf(w, __ldcg(part0 + sp * kPartStride + 65), L);
-      O = fmaf(w, __ldcg(part0 + sp * kPartStride + d), O);
+    for (int sp = ln; sp < n_splits; sp += 32) M = fmaxf(M, __ldcg(part0 + sp * kPartStride + 64));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float L = 0.f, o0 = 0.f, o1 = 0.f;
+    int sp = 0;
+    for (; sp + 4 <= n_splits; sp += 4) {
+      float mv[4], lv[4];
+      float2 av[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float *pp = part0 + (sp + u) * kPartStride;
+        mv[u] = __ldcg(pp + 64);
+        lv[u] = __ldcg(pp + 65);
+        av[u] = __ldcg(reinterpret_cast<const float2 *>(pp + 2 * ln));
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float w = ex2(mv[u] - M);
+        L = fmaf(w, lv[u], L);
+        o0 = fmaf(w, av[u].x, o0);
+        o1 = fmaf(w, av[u].y, o1);
+      }
     }
-    store_out<OutT>(p.o, (int64_t)(rw.row0 + r) * p.o_rs + head * 64 + d, O / L);
+    for (; sp < n_splits; ++sp) {
+      const float *pp = part0 + sp * kPartStride;
+      const float w = ex2(__ldcg(pp + 64) - M);
+      const float2 a = __ldcg(reinterpret_cast<const float2 *>(pp + 2 * ln));
+      L = fmaf(w, __ldcg(pp + 65), L);
+      o0 = fmaf(w, a.x, o0);
+      o1 = fmaf(w, a.y, o1);
+    }
+    const int64_t off = (int64_t)(rw.row0 + r) * p.o_rs + head * 64 + 2 * ln;
+    store_out<OutT>(p.o, off, o0 / L);
+    store_out<OutT>(p.o, off + 1, o1 / L);
   }
   if (tid == 0) p.count[rw.cnt_idx] = 0;  // leave the workspace zeroed for the next call
 }
@@ -805,18 +837,18 @@ bool uses_stream(int q_dtype, int kv_dtype) {
   return kv_dtype != WATTN_F32 && q_dtype == kv_dtype;
 }
 
-// Keys per split. Tensor-core path: as many splits as it takes to give
-// every resident CTA an item (none where there are already enough items),
-// each split at least kStrMinSubs sub-tiles where the keys allow, the splits
-// of a row equal to within a sub-tile. CUDA-core path: the largest chunk
-// (<= 256 keys, 128 for f32 K/V to fit shared memory) that still gives
-// >= ~4 waves of CTAs on 148 SMs.
+// Keys per split. Tensor-core path: no split unless the items number below
+// kStrSplitTarget, then about kStrSplitTarget / items splits, each at least
+// kStrMinSubs sub-tiles where the keys allow, the splits of a row equal to
+// within a sub-tile. CUDA-core path: the largest chunk (<= 256 keys, 128 for
+// f32 K/V to fit shared memory) that still gives >= ~4 waves of CTAs on 148
+// SMs.
 int chunk_for(int q_dtype, int kv_dtype, int ctas_per_chunk_unit, int t_kv) {
   const int subs = std::max(1, (t_kv + kDecSub - 1) / kDecSub);
   if (uses_stream(q_dtype, kv_dtype)) {
-    const long long units = std::max(1, ctas_per_chunk_unit);
-    int splits = (int)std::min<long long>((kStrSlots + units - 1) / units, subs);
-    splits = std::max(1, std::min(splits, subs / kStrMinSubs));
+    const int units = std::max(1, ctas_per_chunk_unit);
+    int splits = std::min(kStrSplitTarget / units, subs / kStrMinSubs);
+    splits = std::max(1, splits);
     return ((subs + splits - 1) / splits) * kDecSub;
   }
   const int max_chunk = (kv_dtype == WATTN_F32 ? 2 : kDecMaxSubs) * kDecSub;
