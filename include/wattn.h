@@ -125,6 +125,32 @@ int wattn_decode_fwd(const void *q, const void *k, const void *v, void *o,
                      float scale, void *workspace, size_t workspace_bytes,
                      void *stream);
 
+/* Cross-attention decode with alignment-head capture: the DTW path of
+ * decode_with_alignment_heads, where multi_head_attention over the encoder
+ * states is followed by capture_cross_attention_heads
+ * (crates/whisper/src/decoder.rs:698-722, 796-828). Same arguments and
+ * output as wattn_decode_fwd, plus the capture, computed from the same dot
+ * products as the attention (one pass over K):
+ *   sel_slot[i], sel_head[i], i < n_sel: the reference's `selected` pairs
+ *     (capture slot, model head); each head at most once per call
+ *     (WATTN_ERR_UNSUPPORTED otherwise), heads < 64;
+ *   capture: device f32, [rows][n_selected][t_kv]; query row r (over all
+ *     groups, r = group * group_size + i) gets, for each selected pair,
+ *     softmax_j(scale * q_r . k_j) at capture[((row_offset + r) * n_selected
+ *     + slot) * t_kv + j]; other slots are left as they are.
+ * The softmax is exact in f32 over the kernel's dot products (the p < 1e-7
+ * skip of the attention output does not apply to the capture, as in the
+ * reference). */
+int wattn_decode_fwd_capture(const void *q, const void *k, const void *v, void *o,
+                             int q_dtype, int kv_dtype, int out_dtype, int n_groups,
+                             int group_size, int t_kv, int n_heads, int d_head,
+                             int64_t q_row_stride, int64_t kv_row_stride,
+                             int64_t kv_group_stride, int64_t o_row_stride,
+                             float scale, void *workspace, size_t workspace_bytes,
+                             const int *sel_slot, const int *sel_head, int n_sel,
+                             int n_selected, int row_offset, float *capture,
+                             void *stream);
+
 /* Decode without any allocation. This entry point has no counterpart in the
  * reference: it exists for callers that may not allocate device memory at
  * all (a real-time audio callback, a host whose allocator is frozen after
@@ -260,6 +286,19 @@ int wattn_multi_head_attention_with_cache(const float *q, const float *k,
                                           size_t total_tokens, size_t t_past,
                                           size_t n_heads, size_t d_model,
                                           float *output);
+
+/* capture_cross_attention_heads (crates/whisper/src/decoder.rs:796-828) on
+ * host f32 slices: q [n_tokens][d_model], k [n_audio][d_model]; for every
+ * (sel_slot[i], sel_head[i]) and token row t, out[((row_offset + t) *
+ * n_selected + slot) * n_audio + j] = softmax_j(q_t . k_j / sqrt(d_head))
+ * over the head's 64 dims; the other slots of `out` are left unchanged.
+ * Runs the fused capture of wattn_decode_fwd_capture. d_model must be
+ * n_heads * 64; heads < 64, each selected at most once. */
+int wattn_capture_cross_attention_heads(const float *q, const float *k, size_t n_tokens,
+                                        size_t n_audio, size_t n_heads, size_t d_model,
+                                        const int *sel_slot, const int *sel_head,
+                                        size_t n_sel, size_t n_selected,
+                                        size_t row_offset, float *out);
 
 /* Batched host-buffer encoder attention: contiguous [batch][t][n_heads*64]
  * host buffers of in_dtype; output [batch][t_q][n_heads*64] of out_dtype. */

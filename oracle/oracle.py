@@ -49,6 +49,9 @@ def lib():
         L.ora_single_token_mha_d64.argtypes = [_f32p, _f32p, _f32p, _sz, _sz, _sz, _f32p]
         L.ora_single_token_mha_d64_scalar.argtypes = [_f32p, _f32p, _f32p, _sz, _sz, _sz, _f32p]
         L.ora_mha_with_cache.argtypes = [_f32p, _f32p, _f32p, _sz, _sz, _sz, _sz, _sz, _f32p]
+        _i32p = ctypes.POINTER(ctypes.c_int)
+        L.ora_capture_heads.argtypes = [_f32p, _f32p, _sz, _sz, _sz, _sz, _i32p, _i32p, _sz, _sz,
+                                        _sz, _f32p]
         L.ora_materialized.argtypes = [_f32p, _f32p, _f32p, _sz, _sz, _sz, _sz, ctypes.c_int, _f32p]
         L.ora_decode_grouped.argtypes = [_f32p, _f32p, _f32p, _sz, _sz, _sz, _sz, _sz, _f32p,
                                          ctypes.c_int]
@@ -101,6 +104,21 @@ def single_token_mha_d64(q, k, v, t_kv, n_heads, d_model, scalar=False):
     out = np.empty(d_model, np.float32)
     fn = lib().ora_single_token_mha_d64_scalar if scalar else lib().ora_single_token_mha_d64
     _check(fn(_p(q), _p(k), _p(v), t_kv, n_heads, d_model, _p(out)), "single_token_mha_d64")
+    return out
+
+
+def capture_heads(q, k, n_tokens, n_audio, n_heads, d_model, selected, n_selected, row_offset,
+                  out):
+    """crates/whisper/src/decoder.rs:796-828 (capture_cross_attention_heads):
+    writes the selected heads' softmax rows into ``out`` (f32, modified in
+    place) at [(row_offset + t) * n_selected + slot][n_audio]."""
+    q, k = _f32(q), _f32(k)
+    assert out.dtype == np.float32 and out.flags.c_contiguous
+    slots = (ctypes.c_int * max(1, len(selected)))(*[int(a) for a, _ in selected])
+    heads = (ctypes.c_int * max(1, len(selected)))(*[int(b) for _, b in selected])
+    _check(lib().ora_capture_heads(_p(q), _p(k), n_tokens, n_audio, n_heads, d_model, slots,
+                                   heads, len(selected), n_selected, row_offset, _p(out)),
+           "capture_cross_attention_heads")
     return out
 
 

@@ -464,6 +464,41 @@ int ora_mha_with_cache(const float *q, const float *k, const float *v,
   return 0;
 }
 
+/* ------------------------------------------- alignment-head capture */
+
+/* crates/whisper/src/decoder.rs:796-828 (capture_cross_attention_heads): for
+ * every token row i and selected (slot, head): score_j = dot_f32(q_i, k_j)
+ * over the head's dims (simd.rs lane order) * 1/sqrt(d_head), softmax_inplace
+ * over the n_audio scores, copied to out[((row_offset + i) * n_selected +
+ * slot) * n_audio ..]. Other slots are not touched. */
+int ora_capture_heads(const float *q, const float *k, size_t n_tokens, size_t n_audio,
+                      size_t n_heads, size_t d_model, const int *sel_slot,
+                      const int *sel_head, size_t n_sel, size_t n_selected,
+                      size_t row_offset, float *out) {
+  if (n_heads == 0 || d_model % n_heads != 0) return -1;
+  size_t d_head = d_model / n_heads;
+  float scale = 1.0f / sqrtf((float)d_head);
+  float *scores = (float *)malloc(sizeof(float) * (n_audio ? n_audio : 1));
+  for (size_t i = 0; i < n_tokens; i++) {
+    for (size_t s = 0; s < n_sel; s++) {
+      if (sel_slot[s] < 0 || (size_t)sel_slot[s] >= n_selected || sel_head[s] < 0 ||
+          (size_t)sel_head[s] >= n_heads) {
+        free(scores);
+        return -1;
+      }
+      size_t ho = (size_t)sel_head[s] * d_head;
+      const float *qv = q + i * d_model + ho;
+      for (size_t j = 0; j < n_audio; j++)
+        scores[j] = dot_f32_avx2order(qv, k + j * d_model + ho, d_head) * scale;
+      ora_softmax_inplace(scores, n_audio);
+      float *dst = out + ((row_offset + i) * n_selected + (size_t)sel_slot[s]) * n_audio;
+      memcpy(dst, scores, sizeof(float) * n_audio);
+    }
+  }
+  free(scores);
+  return 0;
+}
+
 /* ------------------------------------------------- materialized reference */
 
 /* crates/tensor/tests/test_flash_attention_tiled.rs:41-89: full score matrix

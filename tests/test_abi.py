@@ -89,3 +89,24 @@ def test_device_entry_points_validate_first(wattn):
     assert L.wattn_attention_fwd(None, None, None, None, 1, 1, 0, 4, 4, 2, 64, 128, 128, 128, 0, 0,
                                  0, 0.125, 0, 0, None) == 0
     assert L.wattn_decode_workspace_bytes(32, 5, 1500, 20) > 0
+
+
+def test_capture_selection_is_validated_first(wattn):
+    # capture_cross_attention_heads (decoder.rs:796-828) selections that the
+    # fused capture cannot serve are rejected before any CUDA call.
+    q = np.zeros(2 * 128, np.float32)
+    k = np.zeros(10 * 128, np.float32)
+    out = np.zeros(2 * 2 * 10, np.float32)
+    cases = [([(0, 1), (1, 1)], -2),   # one head in two slots
+             ([(2, 0)], -6),           # slot outside n_selected
+             ([(0, 5)], -6)]           # head outside n_heads
+    for sel, status in cases:
+        with pytest.raises(wattn.WattnError) as e:
+            wattn.capture_cross_attention_heads(q, k, 2, 10, 2, 128, sel, 2, 0, out)
+        assert e.value.status == status, sel
+    # d_model != n_heads * 64
+    with pytest.raises(wattn.WattnError) as e:
+        wattn.capture_cross_attention_heads(q, k, 2, 10, 4, 128, [(0, 0)], 2, 0, out)
+    assert e.value.status in (-1, -2)
+    assert (out == 0).all()
+

@@ -225,11 +225,18 @@ int d2h(void *dst, const void *src, size_t n, cudaStream_t st) {
 
 // Ends a host-buffer call: waits for both streams, then reports CUDA errors
 // and the device status word.
+int consume_status();
 int finish_host(HostCtx *h, int rc) {
   for (int i = 0; i < 2; ++i)
     if (cudaStreamSynchronize(h->st[i]) != cudaSuccess && rc == WATTN_OK)
       rc = check_launch("cudaStreamSynchronize");
   if (rc != WATTN_OK) return rc;
+  return consume_status();
+}
+
+// After the device's work is complete: reports (and clears) a bounded wait
+// that ran out, from the current device's status word.
+int consume_status() {
   int *sp = device_status_ptr();
   int s[2] = {WATTN_OK, 0};
   if (sp && cudaMemcpy(s, sp, sizeof(s), cudaMemcpyDeviceToHost) == cudaSuccess &&
@@ -337,7 +344,7 @@ int validate_decode(const void *q, const void *k, const void *v, const void *o, 
 int decode_device(const void *q, const void *k, const void *v, void *o, int q_dt, int kv_dt,
                   int out_dt, int n_groups, int group_size, int t_kv, int n_heads, int64_t q_rs,
                   int64_t kv_rs, int64_t kv_gs, int64_t o_rs, float scale, void *ws,
-                  size_t ws_bytes, cudaStream_t st) {
+                  size_t ws_bytes, cudaStream_t st, const CaptureSpec *cap = nullptr) {
   if (n_groups == 0) return WATTN_OK;
   if (t_kv == 0)
     return launch_zero_rows(o, out_dt, 1, n_groups * group_size, n_heads * kHeadDim, o_rs, 0, st);
@@ -348,7 +355,43 @@ int decode_device(const void *q, const void *k, const void *v, void *o, int q_dt
     ws_bytes = std::max(pl.workspace_bytes, (size_t)1 << 20);
   }
   return launch_decode(q, k, v, o, q_dt, kv_dt, out_dt, n_groups, group_size, t_kv, n_heads, q_rs,
-                       kv_rs, kv_gs, o_rs, scale, ws, ws_bytes, st);
+                       kv_rs, kv_gs, o_rs, scale, ws, ws_bytes, st, cap);
+}
+
+// (slot, head) pairs of an alignment-head capture (decoder.rs:796-828's
+// `selected`) -> CaptureSpec. Each head may be captured once per call.
+int parse_selection(CaptureSpec *cap, const int *sel_slot, const int *sel_head, int n_sel,
+                    int n_selected, int n_heads) {
+  if (n_sel < 0 || n_selected < 0)
+    return set_error(WATTN_ERR_INVALID, "capture: negative count");
+  if (n_sel > 0 && (!sel_slot || !sel_head))
+    return set_error(WATTN_ERR_INVALID, "capture: NULL selection");
+  if (n_sel > 0 && n_heads > 64)
+    return set_error(WATTN_ERR_UNSUPPORTED, "capture: %d heads (at most 64)", n_heads);
+  cap->n_selected = n_selected;
+  for (int h = 0; h < 64; ++h) cap->slot_of_head[h] = -1;
+  for (int i = 0; i < n_sel; ++i) {
+    if (sel_head[i] < 0 || sel_head[i] >= n_heads)
+      return set_error(WATTN_ERR_RANGE, "capture: head %d outside [0, %d)", sel_head[i], n_heads);
+    if (sel_slot[i] < 0 || sel_slot[i] >= n_selected)
+      return set_error(WATTN_ERR_RANGE, "capture: slot %d outside [0, %d)", sel_slot[i],
+                       n_selected);
+    if (cap->slot_of_head[sel_head[i]] >= 0)
+      return set_error(WATTN_ERR_UNSUPPORTED, "capture: head %d selected twice", sel_head[i]);
+    cap->slot_of_head[sel_head[i]] = sel_slot[i];
+  }
+  return WATTN_OK;
+}
+
+int build_capture(CaptureSpec *cap, const int *sel_slot, const int *sel_head, int n_sel,
+                  int n_selected, int row_offset, float *out, int n_heads) {
+  if (row_offset < 0) return set_error(WATTN_ERR_INVALID, "capture: negative row offset");
+  if (n_sel > 0 && !out) return set_error(WATTN_ERR_INVALID, "capture: NULL buffer");
+  if (reinterpret_cast<uintptr_t>(out) & 3)
+    return set_error(WATTN_ERR_INVALID, "capture: buffer must be 4-byte aligned");
+  cap->out = out;
+  cap->row0 = row_offset;
+  return parse_selection(cap, sel_slot, sel_head, n_sel, n_selected, n_heads);
 }
 
 size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -648,6 +691,80 @@ int wattn_multi_head_attention_with_cache(const float *q, const float *k, const 
   const float scale = 1.0f / sqrtf((float)d_head);
   return attention_host(q, k, v, output, WATTN_F32, WATTN_F32, 1, (int)n_tokens,
                         (int)(t_past + n_tokens), (int)n_heads, scale, 1, (int)t_past);
+}
+
+int wattn_decode_fwd_capture(const void *q, const void *k, const void *v, void *o, int q_dtype,
+                             int kv_dtype, int out_dtype, int n_groups, int group_size, int t_kv,
+                             int n_heads, int d_head, int64_t q_row_stride, int64_t kv_row_stride,
+                             int64_t kv_group_stride, int64_t o_row_stride, float scale,
+                             void *workspace, size_t workspace_bytes, const int *sel_slot,
+                             const int *sel_head, int n_sel, int n_selected, int row_offset,
+                             float *capture, void *stream) {
+  clear_error();
+  int rc = validate_decode(q, k, v, o, q_dtype, kv_dtype, out_dtype, n_groups, group_size, t_kv,
+                           n_heads, d_head, q_row_stride, kv_row_stride, kv_group_stride,
+                           o_row_stride, scale);
+  if (rc != WATTN_OK) return rc;
+  CaptureSpec cap;
+  if ((rc = build_capture(&cap, sel_slot, sel_head, n_sel, n_selected, row_offset, capture,
+                          n_heads)) != WATTN_OK)
+    return rc;
+  return decode_device(q, k, v, o, q_dtype, kv_dtype, out_dtype, n_groups, group_size, t_kv,
+                       n_heads, q_row_stride, kv_row_stride, kv_group_stride, o_row_stride, scale,
+                       workspace, workspace_bytes, (cudaStream_t)stream,
+                       n_sel > 0 && t_kv > 0 ? &cap : nullptr);
+}
+
+int wattn_capture_cross_attention_heads(const float *q, const float *k, size_t n_tokens,
+                                        size_t n_audio, size_t n_heads, size_t d_model,
+                                        const int *sel_slot, const int *sel_head, size_t n_sel,
+                                        size_t n_selected, size_t row_offset, float *out) {
+  clear_error();
+  int d_head = 0;
+  int rc = ref_shape(n_heads, d_model, &d_head);
+  if (rc != WATTN_OK) return rc;
+  if (n_tokens > (size_t)INT32_MAX || n_audio > (size_t)INT32_MAX || n_sel > 64 ||
+      n_selected > (size_t)INT32_MAX || row_offset > (size_t)INT32_MAX)
+    return set_error(WATTN_ERR_INVALID, "size too large");
+  CaptureSpec cap;
+  if ((rc = parse_selection(&cap, sel_slot, sel_head, (int)n_sel, (int)n_selected,
+                            (int)n_heads)) != WATTN_OK)
+    return rc;
+  if (n_tokens == 0 || n_sel == 0 || n_audio == 0) return WATTN_OK;
+  if (!q || !k || !out) return set_error(WATTN_ERR_INVALID, "NULL slice");
+  const size_t qb = n_tokens * d_model * 4, kb = n_audio * d_model * 4,
+               cb = n_tokens * n_selected * n_audio * 4;
+  float *host_rows = out + row_offset * n_selected * n_audio;
+  uint8_t *buf = nullptr;
+  if (cudaMalloc(&buf, 2 * qb + kb + cb) != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(WATTN_ERR_NOMEM, "capture: device buffers of %zu bytes", 2 * qb + kb + cb);
+  }
+  float *dq = reinterpret_cast<float *>(buf), *dout = reinterpret_cast<float *>(buf + qb),
+        *dk = reinterpret_cast<float *>(buf + 2 * qb),
+        *dcap = reinterpret_cast<float *>(buf + 2 * qb + kb);
+  // The device buffer holds rows row_offset .. row_offset + n_tokens of `out`.
+  cap.out = dcap;
+  cap.row0 = 0;
+  // Slots not selected keep their contents: the rows go to the device and back.
+  if (cudaMemcpy(dq, q, qb, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(dk, k, kb, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(dcap, host_rows, cb, cudaMemcpyHostToDevice) != cudaSuccess) {
+    rc = check_launch("capture: host to device copy");
+  } else {
+    // The reference's multi_head_attention computes the attention output
+    // beside the capture (decoder.rs:698-722); here V = K only keeps the
+    // launch valid, the output is not returned.
+    rc = decode_device(dq, dk, dk, dout, WATTN_F32, WATTN_F32, WATTN_F32, 1, (int)n_tokens,
+                       (int)n_audio, (int)n_heads, (int64_t)d_model, (int64_t)d_model,
+                       (int64_t)n_audio * d_model, (int64_t)d_model,
+                       1.0f / sqrtf((float)d_head), nullptr, 0, 0, &cap);
+    if (rc == WATTN_OK && cudaMemcpy(host_rows, dcap, cb, cudaMemcpyDeviceToHost) != cudaSuccess)
+      rc = check_launch("capture: device to host copy");
+    if (rc == WATTN_OK) rc = consume_status();
+  }
+  cudaFree(buf);
+  return rc;
 }
 
 int wattn_selftest_bounded_wait(int limit_us, void *stream) {

@@ -42,6 +42,7 @@ constexpr int kDecRows = 8;        // query rows per CTA
 constexpr int kDecThreads = 128;   // CUDA-core path
 constexpr int kDecMaxSubs = 4;     // CUDA-core path: sub-tiles per split (chunk <= 256 keys; 128 for f32)
 constexpr int kPartStride = 66;    // floats per partial: acc[64], m, l
+constexpr int kCapMaxHeads = 64;   // heads an alignment-head capture can select from
 constexpr int kStrStages = 4;      // tensor-core path: depth of the K/V ring (sub-tiles)
 constexpr int kStrWarps = 4;       // compute warps; one more warp issues the loads
 constexpr int kStrThreads = (kStrWarps + 1) * 32;
@@ -60,7 +61,7 @@ constexpr size_t kCounterBytes = (size_t)kMaxSplitCounters * sizeof(int);
 static_assert(kDecSub == kDecSubRows, "paged sub-tiles and TMA boxes must agree");
 // Paged kernels take two tensor maps, DecParams (< 128 bytes) and the table
 // by value; CUDA 12.1+ allows 32764 bytes of kernel parameters.
-static_assert(2 * sizeof(CUtensorMap) + 128 + sizeof(PagedTable) <= 32764,
+static_assert(2 * sizeof(CUtensorMap) + 256 + sizeof(PagedTable) <= 32764,
               "paged kernel parameters exceed the 32764-byte limit");
 
 namespace {
@@ -84,7 +85,21 @@ struct DecParams {
   float *part;   // [rows][n_heads][n_splits][kPartStride]
   int *count;    // [row groups][n_heads]
   int *status;
+  // Alignment-head capture (dense decode only; cap == nullptr turns it off):
+  // the softmax over the keys of each query row r for every head h with
+  // cap_slot[h] >= 0 goes to cap[((cap_row0 + r) * cap_nsel + cap_slot[h]) * t_kv + key].
+  float *cap;
+  int cap_nsel, cap_row0;
+  signed char cap_slot[kCapMaxHeads];
 };
+
+// Capture slot of `head` in this launch, or -1.
+WATTN_DEVINL int cap_slot_of(const DecParams &p, int head) {
+  return (p.cap != nullptr && head < kCapMaxHeads) ? p.cap_slot[head] : -1;
+}
+WATTN_DEVINL float *cap_row(const DecParams &p, int row, int slot) {
+  return p.cap + ((int64_t)(p.cap_row0 + row) * p.cap_nsel + slot) * p.t_kv;
+}
 
 // Shared memory of the CUDA-core path: every sub-tile of the split at once.
 template <int KV_DT>
@@ -339,13 +354,25 @@ WATTN_DEVINL void issue_sub(uint8_t *kdst, uint8_t *vdst, uint64_t *kbar, uint64
   }
 }
 
+// Turns the captured scaled scores of one query row into its softmax over
+// the row's n keys, p = 2^(v - M) / sum 2^(v - M) (one warp; M is any value
+// within 2^8 of the row max, the kernels' running max or the split merge's).
+WATTN_DEVINL void cap_softmax_row(float *row, int n, float M, int ln) {
+  float sum = 0.f;
+  for (int j = ln; j < n; j += 32) sum += ex2(__ldcg(row + j) - M);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float inv = 1.f / sum;
+  for (int j = ln; j < n; j += 32) row[j] = ex2(__ldcg(row + j) - M) * inv;
+}
+
 // Sums the four warps' partial outputs in `red` ([4][kDecRows][64]) and
 // either stores the rows (one split) or writes this split's partial; the
 // last CTA of the (row group, head) to finish then merges every split by
 // log-sum-exp. Called by all threads of the CTA.
 // NAMED: the CTA's compute warps (threads 0..127) call it, synchronising on
 // compute_sync(); otherwise every thread does, on __syncthreads().
-template <typename OutT, bool NAMED>
+template <typename OutT, bool NAMED, bool PAGED>
 __device__ void finish_split(const DecParams &p, const float *red, const float *sm,
                              const float *sl, int *s_last, const DecRows &rw, int head, int split,
                              int n_splits) {
@@ -367,7 +394,16 @@ __device__ void finish_split(const DecParams &p, const float *red, const float *
       }
     }
   }
-  if (n_splits == 1) return;
+  const int n_warps = nt >> 5, wid = tid >> 5, ln = tid & 31;
+  const int cap_slot = PAGED ? -1 : cap_slot_of(p, head);  // no capture on the paged path
+  if (n_splits == 1) {
+    // The captured scores of this CTA's rows were written before the
+    // barriers that precede this call.
+    if (cap_slot >= 0)
+      for (int r = wid; r < rw.nr; r += n_warps)
+        cap_softmax_row(cap_row(p, rw.row0 + r, cap_slot), p.t_kv, sm[r], ln);
+    return;
+  }
 
   // Release: the barrier orders every thread's partial before thread 0's
   // fence, and the fence orders them before the count.
@@ -382,7 +418,6 @@ __device__ void finish_split(const DecParams &p, const float *red, const float *
   if (!*s_last) return;
   // One warp per row, two dims per lane; the splits' partials are read four
   // at a time with independent loads (they sit in L2).
-  const int n_warps = nt >> 5, wid = tid >> 5, ln = tid & 31;
   for (int r = wid; r < rw.nr; r += n_warps) {
     const float *part0 =
         p.part + ((part_base + (int64_t)r * p.n_heads + head) * p.n_splits) * kPartStride;
@@ -421,6 +456,9 @@ __device__ void finish_split(const DecParams &p, const float *red, const float *
     const int64_t off = (int64_t)(rw.row0 + r) * p.o_rs + head * 64 + 2 * ln;
     store_out<OutT>(p.o, off, o0 / L);
     store_out<OutT>(p.o, off + 1, o1 / L);
+    // Every split's captured scores are visible here (they precede each
+    // split's release of the counter).
+    if (cap_slot >= 0) cap_softmax_row(cap_row(p, rw.row0 + r, cap_slot), p.t_kv, M, ln);
   }
   if (tid == 0) p.count[rw.cnt_idx] = 0;  // leave the workspace zeroed for the next call
 }
@@ -535,6 +573,21 @@ __device__ void decode_stream_body(const CUtensorMap &map_k, const CUtensorMap &
       }
       // Mask keys outside [kv_lo, kv_hi) (row g holds keys 2*t4, 2*t4+1 of each 8).
       const int key0 = w.k_beg + st * kDecSub + kb + 2 * t4;
+      if constexpr (!PAGED) {
+        const int slot = cap_slot_of(p, w.head);
+        if (slot >= 0 && g < w.rw.nr) {
+          // Alignment-head capture: the scaled scores (exp2 domain) of the
+          // attended keys; finish_split turns them into the softmax.
+          float *dst = cap_row(p, w.rw.row0 + g, slot);
+#pragma unroll
+          for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int key = key0 + nb * 8 + e;
+              if (key < w.rw.kv_hi) dst[key] = sc[nb][e] * c;
+            }
+        }
+      }
 #pragma unroll
       for (int nb = 0; nb < 2; ++nb)
 #pragma unroll
@@ -615,7 +668,7 @@ __device__ void decode_stream_body(const CUtensorMap &map_k, const CUtensorMap &
     compute_sync();
     if (tid < w.rw.nr) s.l[tid] = s.wl[0][tid] + s.wl[1][tid] + s.wl[2][tid] + s.wl[3][tid];
     compute_sync();
-    finish_split<OutT, true>(p, &s.red[0][0][0], s.m, s.l, &s.last, w.rw, w.head, w.split,
+    finish_split<OutT, true, PAGED>(p, &s.red[0][0][0], s.m, s.l, &s.last, w.rw, w.head, w.split,
                              w.n_splits);
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks)
@@ -673,10 +726,14 @@ __device__ void decode_simt_body(const CUtensorMap &map_k, const CUtensorMap &ma
     half_dots<KV_DT>(s.k[st], krow, half, s.q, nr, dot);
     const int key = k_beg + st * kDecSub + krow;
     const bool valid = key >= rw.kv_lo && key < rw.kv_hi;
+    const int slot = PAGED ? -1 : cap_slot_of(p, head);
 #pragma unroll
     for (int r = 0; r < kDecRows; ++r) {
       const float full = dot[r] + __shfl_xor_sync(0xffffffffu, dot[r], 1);
-      if (half == 0 && r < nr) s.sc[r][st * kDecSub + krow] = valid ? full : -INFINITY;
+      if (half == 0 && r < nr) {
+        s.sc[r][st * kDecSub + krow] = valid ? full : -INFINITY;
+        if (slot >= 0 && valid) cap_row(p, rw.row0 + r, slot)[key] = full;  // alignment-head capture
+      }
     }
   }
   __syncthreads();
@@ -731,7 +788,7 @@ __device__ void decode_simt_body(const CUtensorMap &map_k, const CUtensorMap &ma
       *reinterpret_cast<float2 *>(&red[(warp * kDecRows + r) * 64 + 2 * lane]) =
           make_float2(acc[r][0], acc[r][1]);
   __syncthreads();
-  finish_split<OutT, false>(p, red, s.m, s.l, &s.last, rw, head, split, n_splits);
+  finish_split<OutT, false, PAGED>(p, red, s.m, s.l, &s.last, rw, head, split, n_splits);
 }
 
 template <int Q_DT, int KV_DT>
@@ -753,14 +810,14 @@ __global__ void __launch_bounds__(kDecThreads)
 }
 
 template <int DT, int OUT_DT>
-__global__ void __launch_bounds__(kStrThreads)
+__global__ void __launch_bounds__(kStrThreads, 3)  // three CTAs per SM (shared memory allows three)
     decode_stream_dense_kernel(const __grid_constant__ CUtensorMap map_k,
                                const __grid_constant__ CUtensorMap map_v, const DecParams p) {
   decode_stream_body<DT, OUT_DT, false>(map_k, map_v, p, nullptr);
 }
 
 template <int DT, int OUT_DT>
-__global__ void __launch_bounds__(kStrThreads)
+__global__ void __launch_bounds__(kStrThreads, 3)  // three CTAs per SM (shared memory allows three)
     decode_stream_paged_kernel(const __grid_constant__ CUtensorMap map_k,
                                const __grid_constant__ CUtensorMap map_v, const DecParams p,
                                const __grid_constant__ PagedTable pt) {
@@ -885,7 +942,11 @@ DecodePlan plan_decode(int n_groups, int group_size, int t_kv, int n_heads, int 
 int launch_decode(const void *q, const void *k, const void *v, void *o, int q_dtype,
                   int kv_dtype, int out_dtype, int n_groups, int group_size, int t_kv,
                   int n_heads, int64_t q_rs, int64_t kv_rs, int64_t kv_gs, int64_t o_rs,
-                  float scale, void *workspace, size_t workspace_bytes, cudaStream_t stream) {
+                  float scale, void *workspace, size_t workspace_bytes, cudaStream_t stream,
+                  const CaptureSpec *cap) {
+  if (cap != nullptr && n_heads > kCapMaxHeads)
+    return set_error(WATTN_ERR_UNSUPPORTED, "decode capture: %d heads (at most %d)", n_heads,
+                     kCapMaxHeads);
   const DecodePlan pl = plan_decode(n_groups, group_size, t_kv, n_heads, q_dtype, kv_dtype);
   if (pl.n_splits > 1 && workspace_bytes < pl.workspace_bytes)
     return set_error(WATTN_ERR_INVALID, "decode: workspace of %zu bytes, %zu needed",
@@ -921,6 +982,15 @@ int launch_decode(const void *q, const void *k, const void *v, void *o, int q_dt
   p.part = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(workspace) + kCounterBytes);
   p.status = device_status_ptr();
   if (p.status == nullptr) return WATTN_ERR_CUDA;
+  p.cap = nullptr;
+  p.cap_nsel = p.cap_row0 = 0;
+  for (int h = 0; h < kCapMaxHeads; ++h) p.cap_slot[h] = -1;
+  if (cap != nullptr) {
+    p.cap = cap->out;
+    p.cap_nsel = cap->n_selected;
+    p.cap_row0 = cap->row0;
+    for (int h = 0; h < n_heads; ++h) p.cap_slot[h] = (signed char)cap->slot_of_head[h];
+  }
   p.n_items = pl.n_splits * n_heads * n_groups * pl.row_chunks;
   const dim3 grid = uses_stream(q_dtype, kv_dtype)
                         ? dim3(stream_grid(p.n_items))
@@ -959,6 +1029,9 @@ int launch_decode_paged(const CUtensorMap &map_k, const CUtensorMap &map_v, cons
   p.part = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(workspace) + kCounterBytes);
   p.status = device_status_ptr();
   if (p.status == nullptr) return WATTN_ERR_CUDA;
+  p.cap = nullptr;  // no capture on the paged (self-attention) path
+  p.cap_nsel = p.cap_row0 = 0;
+  for (int h = 0; h < kCapMaxHeads; ++h) p.cap_slot[h] = -1;
   p.n_items = p.n_splits * n_heads * pt.n_rows;
   const dim3 grid = !uses_stream(q_dtype, kv_dtype) ? dim3(p.n_splits, n_heads, pt.n_rows)
                     : kStrPagedPersist              ? dim3(stream_grid(p.n_items))

@@ -65,10 +65,19 @@ struct DecodePlan {
 };
 DecodePlan plan_decode(int n_groups, int group_size, int t_kv, int n_heads, int q_dtype,
                        int kv_dtype);
+// Alignment-head capture of a dense decode launch: for every query row r
+// and head h with slot_of_head[h] >= 0, the softmax over the t_kv keys is
+// written to out[((row0 + r) * n_selected + slot_of_head[h]) * t_kv + key].
+struct CaptureSpec {
+  float *out;  // device
+  int n_selected, row0;
+  int slot_of_head[64];
+};
 int launch_decode(const void *q, const void *k, const void *v, void *o, int q_dtype,
                   int kv_dtype, int out_dtype, int n_groups, int group_size, int t_kv,
                   int n_heads, int64_t q_rs, int64_t kv_rs, int64_t kv_gs, int64_t o_rs,
-                  float scale, void *workspace, size_t workspace_bytes, cudaStream_t stream);
+                  float scale, void *workspace, size_t workspace_bytes, cudaStream_t stream,
+                  const CaptureSpec *cap = nullptr);
 
 // ----------------------------------------------------------- paged decode
 constexpr int kDecSubRows = 64;     // keys per decode sub-tile (TMA box rows)

@@ -64,6 +64,9 @@ _SIGS = {
                               _i64, _i64, _i64, _i64, _f, _vp, _sz, _vp]),
     "wattn_decode_fwd_noalloc": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i,
                                       _i64, _i64, _i64, _i64, _f, _vp]),
+    "wattn_decode_fwd_capture": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i,
+                                      _i64, _i64, _i64, _i64, _f, _vp, _sz, _ip, _ip, _i, _i, _i,
+                                      _vp, _vp]),
     "wattn_kv_create": (_i, [ctypes.POINTER(_vp), _i, _i, _i, _i, _i, _i, _i, _i]),
     "wattn_kv_destroy": (_i, [_vp]),
     "wattn_kv_clear": (_i, [_vp]),
@@ -84,6 +87,8 @@ _SIGS = {
     "wattn_multi_head_attention": (_i, [_fp, _fp, _fp, _sz, _sz, _sz, _sz, _i, _fp]),
     "wattn_single_token_mha_d64": (_i, [_fp, _fp, _fp, _sz, _sz, _sz, _fp]),
     "wattn_multi_head_attention_with_cache": (_i, [_fp, _fp, _fp, _sz, _sz, _sz, _sz, _sz, _fp]),
+    "wattn_capture_cross_attention_heads": (_i, [_fp, _fp, _sz, _sz, _sz, _sz, _ip, _ip, _sz, _sz,
+                                                 _sz, _fp]),
     "wattn_attention_host": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _i]),
     "wattn_decode_host": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f]),
     "wattn_selftest_bounded_wait": (_i, [_i, _vp]),
@@ -179,6 +184,26 @@ def multi_head_attention_with_cache(q, k, v, n_tokens, total_tokens, t_past, n_h
            "multi_head_attention_with_cache")
 
 
+def capture_cross_attention_heads(q, k, n_tokens, n_audio, n_heads, d_model, selected,
+                                  n_selected, row_offset, out) -> None:
+    """decoder.rs:796 ``capture_cross_attention_heads``: for each (slot, head)
+    in ``selected`` and token row t, out[row_offset + t][slot][:] = the
+    softmax over the n_audio keys of q_t . k / sqrt(d_head) for that head."""
+    q, k, out = (_f32_host(x, n) for x, n in ((q, "q"), (k, "k"), (out, "out")))
+    _expect_len(q, n_tokens * d_model, "q")
+    _expect_len(k, n_audio * d_model, "k")
+    if out.size < (row_offset + n_tokens) * n_selected * n_audio:
+        raise WattnError(f"out: {out.size} elements, "
+                         f"{(row_offset + n_tokens) * n_selected * n_audio} needed")
+    slots = [int(a) for a, _ in selected]
+    heads = [int(b) for _, b in selected]
+    _check(lib.wattn_capture_cross_attention_heads(_fptr(q), _fptr(k), n_tokens, n_audio, n_heads,
+                                                   d_model, _iarr(slots), _iarr(heads),
+                                                   len(selected), n_selected, row_offset,
+                                                   _fptr(out)),
+           "capture_cross_attention_heads")
+
+
 def _dt_of(a) -> int:
     name = str(a.dtype).rsplit(".", 1)[-1]  # "torch.bfloat16" / numpy "float32"
     if name == "float32":
@@ -267,6 +292,28 @@ def decode_fwd(q, k, v, o, *, n_groups, group_size, t_kv, n_heads, scale, q_row_
                                 n_groups, group_size, t_kv, n_heads, 64, q_row_stride or w, kv_rs,
                                 kv_gs, o_row_stride or w, scale, ws_ptr, ws_bytes,
                                 _stream_ptr(stream)), "decode_fwd")
+
+
+def decode_fwd_capture(q, k, v, o, *, n_groups, group_size, t_kv, n_heads, scale, selected,
+                       n_selected, capture, row_offset=0, q_row_stride=None, kv_row_stride=None,
+                       kv_group_stride=None, o_row_stride=None, workspace=None,
+                       stream=None) -> None:
+    """``wattn_decode_fwd_capture``: decode_fwd plus the alignment-head
+    capture; ``selected`` lists (slot, head) pairs, ``capture`` is a CUDA f32
+    tensor [rows][n_selected][t_kv] (rows from row_offset)."""
+    w = n_heads * 64
+    kv_rs = kv_row_stride or w
+    kv_gs = kv_group_stride if kv_group_stride is not None else t_kv * kv_rs
+    ws_ptr = _dev(workspace) if workspace is not None else None
+    ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    slots = [int(a) for a, _ in selected]
+    heads = [int(b) for _, b in selected]
+    _check(lib.wattn_decode_fwd_capture(_dev(q), _dev(k), _dev(v), _dev(o), _dt_of(q), _dt_of(k),
+                                        _dt_of(o), n_groups, group_size, t_kv, n_heads, 64,
+                                        q_row_stride or w, kv_rs, kv_gs, o_row_stride or w, scale,
+                                        ws_ptr, ws_bytes, _iarr(slots), _iarr(heads),
+                                        len(selected), n_selected, row_offset, _dev(capture),
+                                        _stream_ptr(stream)), "decode_fwd_capture")
 
 
 def decode_fwd_noalloc(q, k, v, o, *, n_groups, group_size, t_kv, n_heads, scale,
