@@ -542,12 +542,30 @@ __device__ void decode_stream_body(const CUtensorMap &map_k, const CUtensorMap &
   const float c = p.scale_log2;
   const int kb = warp * 16;
   uint32_t pos = 0;  // position in the ring, as the producer counts it
+  // Each item's description and query rows are fetched one item ahead, at
+  // the start of the previous item, so their latency (a page-table entry in
+  // the constant bank, a query row in HBM) hides behind a whole item.
   uint32_t qa[4][4], qn[4][4];
-  int q_item = -1;   // item whose query rows qa holds
+  DecWork w;
+  if (blockIdx.x < p.n_items) {
+    w = dec_item<PAGED>(p, pt, blockIdx.x);
+    if (w.n_sub > 0) load_q<DT>(qa, p, w.rw, w.head, g, t4);
+  }
   for (int it = blockIdx.x; it < p.n_items; it += gridDim.x) {
-    const DecWork w = dec_item<PAGED>(p, pt, it);
-    if (w.n_sub == 0) continue;  // a paged row with fewer splits than the longest
-    if (q_item != it) load_q<DT>(qa, p, w.rw, w.head, g, t4);
+    const int nx = it + gridDim.x;
+    DecWork wn;
+    if (nx < p.n_items) {
+      wn = dec_item<PAGED>(p, pt, nx);
+      if (wn.n_sub > 0) load_q<DT>(qn, p, wn.rw, wn.head, g, t4);
+    }
+    if (w.n_sub == 0) {  // a paged row with fewer splits than the longest
+      w = wn;
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) qa[ks][e] = qn[ks][e];
+      continue;
+    }
     float m_r = -INFINITY, l_r = 0.f;
     float acc[8][4];
 #pragma unroll
@@ -642,12 +660,6 @@ __device__ void decode_stream_body(const CUtensorMap &map_k, const CUtensorMap &
     l_r += __shfl_xor_sync(0xffffffffu, l_r, 1);
     l_r += __shfl_xor_sync(0xffffffffu, l_r, 2);
 
-    // The next item's query rows load while this item's epilogue runs.
-    const int nx = it + gridDim.x;
-    if (nx < p.n_items) {
-      const DecWork wn = dec_item<PAGED>(p, pt, nx);
-      load_q<DT>(qn, p, wn.rw, wn.head, g, t4);
-    }
 
     // ---- merge the four compute warps (log-sum-exp) into red / s.m / s.l
     compute_sync();  // the previous item's epilogue is done with red, m, l
@@ -670,11 +682,11 @@ __device__ void decode_stream_body(const CUtensorMap &map_k, const CUtensorMap &
     compute_sync();
     finish_split<OutT, true, PAGED>(p, &s.red[0][0][0], s.m, s.l, &s.last, w.rw, w.head, w.split,
                              w.n_splits);
+    w = wn;
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks)
 #pragma unroll
       for (int e = 0; e < 4; ++e) qa[ks][e] = qn[ks][e];
-    q_item = nx;
   }
 }
 
