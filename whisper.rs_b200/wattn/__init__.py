@@ -344,8 +344,11 @@ def selftest_bounded_wait(limit_us: int = 1000, stream=None) -> int:
 
 
 def _iarr(xs):
-    arr = (ctypes.c_int * max(1, len(xs)))(*xs)
-    return arr
+    """Int list -> int* argument. A C-contiguous int32 numpy array is passed
+    without copying (build it once when the same list goes to every call)."""
+    if isinstance(xs, np.ndarray) and xs.dtype == np.int32 and xs.flags.c_contiguous:
+        return xs.ctypes.data_as(_ip)
+    return (ctypes.c_int * max(1, len(xs)))(*xs)
 
 
 class DeviceKvCache:
