@@ -140,3 +140,28 @@ def test_softmax_inplace(oracle):
     y = oracle.softmax_inplace(x)
     e = np.exp(x.astype(np.float64) - x.max())
     assert np.abs(y - e / e.sum()).max() < 1e-7
+
+
+def test_capture_heads_is_the_softmax_of_the_scaled_dots(oracle):
+    """capture_cross_attention_heads (decoder.rs:796-828): each captured row is
+    softmax_j(q . k_j / sqrt(d_head)) of the selected head, laid out
+    [row][slot][n_audio]; unselected slots are left alone. Checked against a
+    float64 evaluation of that formula."""
+    rng = np.random.default_rng(5)
+    n_tokens, n_audio, n_heads, d_head = 3, 257, 4, 64
+    d = n_heads * d_head
+    q = rng.standard_normal(n_tokens * d).astype(np.float32)
+    k = rng.standard_normal(n_audio * d).astype(np.float32)
+    selected, n_selected, row_offset = [(2, 3), (0, 1)], 3, 1
+    out = np.full((row_offset + n_tokens) * n_selected * n_audio, -1.0, np.float32)
+    oracle.capture_heads(q, k, n_tokens, n_audio, n_heads, d, selected, n_selected, row_offset, out)
+    out = out.reshape(-1, n_selected, n_audio)
+    q64 = q.reshape(n_tokens, n_heads, d_head).astype(np.float64)
+    k64 = k.reshape(n_audio, n_heads, d_head).astype(np.float64)
+    for slot, head in selected:
+        s = q64[:, head] @ k64[:, head].T / np.sqrt(d_head)
+        p = np.exp(s - s.max(-1, keepdims=True))
+        p /= p.sum(-1, keepdims=True)
+        assert np.abs(out[row_offset:, slot] - p).max() < 1e-6
+    assert (out[:, 1] == -1.0).all() and (out[0] == -1.0).all()
+
