@@ -211,6 +211,17 @@ int wattn_kv_clear_slot(wattn_kv_cache *cache, int slot);  /* :176-186 */
 int wattn_kv_ensure_slots(wattn_kv_cache *cache, int n_slots); /* :203-214 */
 int wattn_kv_copy_slot(wattn_kv_cache *cache, int dst, int src,
                        void *stream);                      /* :220-234 */
+
+/* The slot assignment of BeamSearch::step (crates/whisper/src/beam.rs:418-460)
+ * as one call: parent_slot[i] is the slot of retained branch i (in ranking
+ * order). Every parent slot is reserved; the first child of a parent keeps
+ * its slot, each further child gets the lowest free slot at or after the
+ * previous one and a fork of its parent (copy_slot: the pages are shared,
+ * nothing is copied until a write). out_slot[i] receives branch i's slot.
+ * WATTN_ERR_RANGE if the slots run out (the reference panics: "beam slot
+ * arena exhausted"); the cache is then unchanged. */
+int wattn_kv_assign_beams(wattn_kv_cache *cache, const int *parent_slot,
+                          int n_branches, int *out_slot);
 int wattn_kv_slot_len(const wattn_kv_cache *cache, int slot,
                       int *len);                           /* :237-239 */
 int wattn_kv_slide_to_fit(wattn_kv_cache *cache, int slot, int n_new,

@@ -45,6 +45,34 @@ class DecoderKvCacheOracle:
                 self.v_self[layer].append(np.zeros((0, self.d_model), np.float32))
             self.t_past.append(0)
 
+    def assign_beams(self, parent_slots):
+        """crates/whisper/src/beam.rs:418-460 (the slot hand-out at the end of
+        BeamSearch::step), applied to this cache: returns each branch's slot."""
+        n_slots = len(self.t_past)
+        reserved = [False] * n_slots
+        for p in parent_slots:
+            if not p < n_slots:
+                raise IndexError(f"slot {p} out of range")
+            reserved[p] = True
+        claimed = [False] * n_slots
+        out = []
+        free_cursor = 0
+        for parent in parent_slots:
+            if not claimed[parent]:
+                claimed[parent] = True
+                out.append(parent)
+                continue
+            new_slot = free_cursor
+            while new_slot < n_slots and (reserved[new_slot] or claimed[new_slot]):
+                new_slot += 1
+            if new_slot >= n_slots:
+                raise RuntimeError("beam slot arena exhausted")
+            claimed[new_slot] = True
+            self.copy_slot(new_slot, parent)
+            out.append(new_slot)
+            free_cursor = new_slot
+        return out
+
     def copy_slot(self, dst: int, src: int):  # :220-234
         if not dst < len(self.t_past):
             raise IndexError(f"slot {dst} out of range")

@@ -167,6 +167,32 @@ def test_append_row_layouts(W, src, dst, pad):
     c.close()
 
 
+def test_assign_beams(W, oracle):
+    """BeamSearch::step's slot hand-out (beam.rs:418-460) on the device cache
+    against the host model: same slots, same rows, and appends after a
+    multi-way fork land copy-on-write in the right slots."""
+    h = Harness(W, oracle, 1, n_layers=2, n_slots=8, n_heads=3, max_ctx=300)
+    h.step([0], [70])
+    for dst in (2, 4):
+        h.dev.copy_slot(dst, 0)
+        h.ref.copy_slot(dst, 0)
+    h.step([0, 2, 4], [5, 9, 1])         # three diverged beams
+    parents = [2, 0, 2, 2, 4]
+    got = h.dev.assign_beams(parents)
+    assert got == h.ref.assign_beams(parents) == [2, 0, 1, 3, 4]
+    h.check_rows()
+    h.step(got, [1] * len(got))          # every retained beam appends a token
+    h.step([1, 3], [2, 1])
+    # more branches than slots: rejected, nothing changes
+    used = h.dev.stats()[0]
+    lens = [h.dev.slot_len(s) for s in range(8)]
+    with pytest.raises(W.WattnError) as e:
+        h.dev.assign_beams([0] * 9)
+    assert e.value.status == -6
+    assert h.dev.stats()[0] == used and [h.dev.slot_len(s) for s in range(8)] == lens
+    h.check_rows()
+
+
 def test_cache_errors(W):
     c = W.DeviceKvCache(1, 2, 2, 128)
     with pytest.raises(W.WattnError) as e:

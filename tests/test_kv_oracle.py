@@ -49,3 +49,22 @@ def test_copy_slot_rewind_and_clear():
         c.copy_slot(7, 0)
     c.clear()
     assert c.t_past == [0] * 5
+
+
+def test_assign_beams_follows_the_reference_slot_hand_out():
+    """beam.rs:418-460 worked by hand: parents [2, 0, 2, 2, 4] over 8 slots.
+    Reserved {0, 2, 4}; branches 0, 1 and 4 keep their parents' slots, the two
+    extra children of slot 2 take the free slots 1 and 3 and fork it."""
+    import numpy as np
+    from oracle.kv_cache_oracle import DecoderKvCacheOracle
+    c = DecoderKvCacheOracle(1, 8, 4)
+    for s, n in ((0, 3), (2, 5), (4, 1)):
+        c.append(0, s, np.full((n, 4), s, np.float32), np.full((n, 4), -s, np.float32))
+        c.advance(s, n)
+    assert c.assign_beams([2, 0, 2, 2, 4]) == [2, 0, 1, 3, 4]
+    for s in (1, 3):
+        assert c.t_past[s] == 5 and (c.k_self[0][s] == 2).all() and (c.v_self[0][s] == -2).all()
+    assert c.t_past[5:] == [0, 0, 0]
+    with pytest.raises(RuntimeError):
+        c.assign_beams([0] * 9)  # nine branches on eight slots
+

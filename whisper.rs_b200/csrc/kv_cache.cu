@@ -331,15 +331,11 @@ int wattn_kv_ensure_slots(wattn_kv_cache *c, int n_slots) {
   return WATTN_OK;
 }
 
-int wattn_kv_copy_slot(wattn_kv_cache *c, int dst, int src, void *stream) {
-  clear_error();
-  (void)stream;  // a fork only shares pages; copies happen at the next write
-  if (!c) return set_error(WATTN_ERR_INVALID, "kv_copy_slot: NULL cache");
-  std::lock_guard<std::mutex> lk(c->mu);
-  int rc = c->check_slot(dst);
-  if (rc) return rc;
-  if ((rc = c->check_slot(src))) return rc;
-  if (dst == src) return WATTN_OK;
+namespace {
+// copy_slot with the cache locked and both slots checked: dst shares src's
+// pages (reference counts); copies happen at the next write.
+void fork_slot(wattn_kv_cache *c, int dst, int src) {
+  if (dst == src) return;
   auto &d = c->slots[dst];
   const auto &s = c->slots[src];
   // Keep the source's pages alive before the destination drops its own
@@ -357,6 +353,62 @@ int wattn_kv_copy_slot(wattn_kv_cache *c, int dst, int src, void *stream) {
   d.pages = std::move(pages);
   d.start = start;
   d.t_past = d.stored = t;
+}
+}  // namespace
+
+int wattn_kv_copy_slot(wattn_kv_cache *c, int dst, int src, void *stream) {
+  clear_error();
+  (void)stream;  // a fork only shares pages; copies happen at the next write
+  if (!c) return set_error(WATTN_ERR_INVALID, "kv_copy_slot: NULL cache");
+  std::lock_guard<std::mutex> lk(c->mu);
+  int rc = c->check_slot(dst);
+  if (rc) return rc;
+  if ((rc = c->check_slot(src))) return rc;
+  fork_slot(c, dst, src);
+  return WATTN_OK;
+}
+
+int wattn_kv_assign_beams(wattn_kv_cache *c, const int *parent_slot, int n_branches,
+                          int *out_slot) {
+  clear_error();
+  if (!c) return set_error(WATTN_ERR_INVALID, "kv_assign_beams: NULL cache");
+  if (n_branches < 0 || (n_branches > 0 && (!parent_slot || !out_slot)))
+    return set_error(WATTN_ERR_INVALID, "kv_assign_beams: NULL or negative argument");
+  std::lock_guard<std::mutex> lk(c->mu);
+  const int n_slots = (int)c->slots.size();
+  // Every retained branch's parent slot is reserved up front, so a sibling's
+  // extra child cannot take the slot its owner is about to claim.
+  std::vector<char> reserved(n_slots, 0), claimed(n_slots, 0);
+  for (int i = 0; i < n_branches; ++i) {
+    int rc = c->check_slot(parent_slot[i]);
+    if (rc) return rc;
+    reserved[parent_slot[i]] = 1;
+  }
+  // The first child of a parent keeps its slot; each further child forks
+  // the parent into the next free slot. Planned first, so an exhausted
+  // arena changes nothing.
+  std::vector<int> plan(n_branches);
+  int free_cursor = 0;
+  for (int i = 0; i < n_branches; ++i) {
+    const int parent = parent_slot[i];
+    if (!claimed[parent]) {
+      claimed[parent] = 1;
+      plan[i] = parent;
+      continue;
+    }
+    int ns = free_cursor;
+    while (ns < n_slots && (reserved[ns] || claimed[ns])) ++ns;
+    if (ns >= n_slots)
+      return set_error(WATTN_ERR_RANGE, "kv_assign_beams: beam slot arena exhausted (%d slots)",
+                       n_slots);
+    claimed[ns] = 1;
+    plan[i] = ns;
+    free_cursor = ns;
+  }
+  for (int i = 0; i < n_branches; ++i) {
+    if (plan[i] != parent_slot[i]) fork_slot(c, plan[i], parent_slot[i]);
+    out_slot[i] = plan[i];
+  }
   return WATTN_OK;
 }
 

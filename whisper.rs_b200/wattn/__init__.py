@@ -73,6 +73,7 @@ _SIGS = {
     "wattn_kv_clear_slot": (_i, [_vp, _i]),
     "wattn_kv_ensure_slots": (_i, [_vp, _i]),
     "wattn_kv_copy_slot": (_i, [_vp, _i, _i, _vp]),
+    "wattn_kv_assign_beams": (_i, [_vp, _ip, _i, _ip]),
     "wattn_kv_slot_len": (_i, [_vp, _i, _ip]),
     "wattn_kv_slide_to_fit": (_i, [_vp, _i, _i, _i, _ip]),
     "wattn_kv_set_t_past": (_i, [_vp, _i, _i]),
@@ -387,6 +388,14 @@ class DeviceKvCache:
 
     def copy_slot(self, dst, src, stream=None):
         _check(lib.wattn_kv_copy_slot(self._h, dst, src, _stream_ptr(stream)), "kv_copy_slot")
+
+    def assign_beams(self, parent_slots) -> list:
+        """beam.rs:418-460: slots for the retained branches whose parents are
+        ``parent_slots`` (ranking order), forking where a parent has several."""
+        n = len(parent_slots)
+        out = (ctypes.c_int * max(1, n))()
+        _check(lib.wattn_kv_assign_beams(self._h, _iarr(parent_slots), n, out), "kv_assign_beams")
+        return list(out[:n])
 
     def slot_len(self, slot) -> int:
         n = ctypes.c_int(0)
