@@ -151,6 +151,29 @@ int wattn_decode_fwd_capture(const void *q, const void *k, const void *v, void *
                              int n_selected, int row_offset, float *capture,
                              void *stream);
 
+/* Linear projection y = x W^T (+ bias) on the tensor cores: Weight::linear
+ * (crates/tensor/src/weight.rs:121, ops/matmul.rs:4-110: output[t][r] =
+ * sum_c x[t][c] W[r][c] + bias[r]) with 16-bit x and W (both in_dtype:
+ * f16 or bf16; f32 accumulation). x [m][k] (row stride x_row_stride), W
+ * [n][k] (w_row_stride), y [m][n] (y_row_stride) in out_dtype; bias: device
+ * f32 [n] or NULL. x and W must be 16-byte aligned with row strides whose
+ * byte size is a multiple of 16. */
+int wattn_linear_fwd(const void *x, const void *w, const float *bias, void *y,
+                     int in_dtype, int out_dtype, int m, int n, int k,
+                     int64_t x_row_stride, int64_t w_row_stride,
+                     int64_t y_row_stride, void *stream);
+
+/* precompute_cross_attn for one layer (crates/whisper/src/decoder.rs:423-447)
+ * on the device: k_out = enc Wk^T and v_out = enc Wv^T + bv, [n_tokens]
+ * [d_model] each (row stride kv_row_stride), with Wk, Wv [d_model][d_model]
+ * in in_dtype and bv device f32 [d_model]. The outputs are the K and V that
+ * wattn_decode_fwd reads for one utterance (n_tokens = its encoder states). */
+int wattn_cross_kv_project(const void *enc, const void *wk, const void *wv,
+                           const float *bv, void *k_out, void *v_out,
+                           int in_dtype, int out_dtype, int n_tokens, int d_model,
+                           int64_t enc_row_stride, int64_t kv_row_stride,
+                           void *stream);
+
 /* Decode without any allocation. This entry point has no counterpart in the
  * reference: it exists for callers that may not allocate device memory at
  * all (a real-time audio callback, a host whose allocator is frozen after

@@ -49,6 +49,7 @@ def lib():
         L.ora_single_token_mha_d64.argtypes = [_f32p, _f32p, _f32p, _sz, _sz, _sz, _f32p]
         L.ora_single_token_mha_d64_scalar.argtypes = [_f32p, _f32p, _f32p, _sz, _sz, _sz, _f32p]
         L.ora_mha_with_cache.argtypes = [_f32p, _f32p, _f32p, _sz, _sz, _sz, _sz, _sz, _f32p]
+        L.ora_linear.argtypes = [_f32p, _f32p, _f32p, _sz, _sz, _sz, _f32p, ctypes.c_int]
         _i32p = ctypes.POINTER(ctypes.c_int)
         L.ora_capture_heads.argtypes = [_f32p, _f32p, _sz, _sz, _sz, _sz, _i32p, _i32p, _sz, _sz,
                                         _sz, _f32p]
@@ -105,6 +106,16 @@ def single_token_mha_d64(q, k, v, t_kv, n_heads, d_model, scalar=False):
     fn = lib().ora_single_token_mha_d64_scalar if scalar else lib().ora_single_token_mha_d64
     _check(fn(_p(q), _p(k), _p(v), t_kv, n_heads, d_model, _p(out)), "single_token_mha_d64")
     return out
+
+
+def linear(x, w, bias, m, n, k, n_threads=None):
+    """crates/tensor/src/ops/matmul.rs:4-110: y = x W^T (+ bias), f32."""
+    x, w = _f32(x), _f32(w)
+    b = _f32(bias) if bias is not None else None
+    y = np.empty(m * n, np.float32)
+    _check(lib().ora_linear(_p(x), _p(w), _p(b) if b is not None else None, m, n, k, _p(y),
+                            n_threads or os.cpu_count() or 1), "linear")
+    return y
 
 
 def capture_heads(q, k, n_tokens, n_audio, n_heads, d_model, selected, n_selected, row_offset,

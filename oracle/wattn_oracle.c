@@ -464,6 +464,56 @@ int ora_mha_with_cache(const float *q, const float *k, const float *v,
   return 0;
 }
 
+/* ------------------------------------------------------------ linear */
+
+/* crates/tensor/src/ops/matmul.rs:4-110 (linear / linear_parallel):
+ * output[t][r] = sum_c input[t][c] * weight[r][c] (+ bias[r]), in_features
+ * = k, out_features = n, num_tokens = m. The reference hands the m >= 16
+ * case to matrixmultiply::sgemm (third-party, not vendored); its summation
+ * order is restated as one f32 FMA chain per output. Rows spread over
+ * n_threads. */
+typedef struct {
+  const float *x, *w, *bias;
+  float *y;
+  size_t m, n, k, r0, r1;
+} LinJob;
+
+static void *linear_rows(void *arg) {
+  LinJob *j = (LinJob *)arg;
+  for (size_t t = j->r0; t < j->r1; t++)
+    for (size_t r = 0; r < j->n; r++) {
+      const float *xr = j->x + t * j->k, *wr = j->w + r * j->k;
+      float acc = 0.f;
+      for (size_t c = 0; c < j->k; c++) acc = fmaf(xr[c], wr[c], acc);
+      j->y[t * j->n + r] = acc + (j->bias ? j->bias[r] : 0.f);
+    }
+  return NULL;
+}
+
+int ora_linear(const float *x, const float *w, const float *bias, size_t m, size_t n, size_t k,
+               float *y, int n_threads) {
+  if (n_threads < 1) n_threads = 1;
+  if (n_threads > 64) n_threads = 64;
+  pthread_t th[64];
+  LinJob jobs[64];
+  size_t per = (m + n_threads - 1) / n_threads;
+  int started = 0;
+  for (int i = 0; i < n_threads; i++) {
+    size_t r0 = i * per, r1 = r0 + per > m ? m : r0 + per;
+    if (r0 >= r1) break;
+    jobs[i] = (LinJob){x, w, bias, y, m, n, k, r0, r1};
+    if (pthread_create(&th[i], NULL, linear_rows, &jobs[i]) != 0) {
+      linear_rows(&jobs[i]);
+      jobs[i].r0 = jobs[i].r1;
+      th[i] = 0;
+    }
+    started = i + 1;
+  }
+  for (int i = 0; i < started; i++)
+    if (th[i]) pthread_join(th[i], NULL);
+  return 0;
+}
+
 /* ------------------------------------------- alignment-head capture */
 
 /* crates/whisper/src/decoder.rs:796-828 (capture_cross_attention_heads): for

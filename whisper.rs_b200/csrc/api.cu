@@ -767,6 +767,54 @@ int wattn_capture_cross_attention_heads(const float *q, const float *k, size_t n
   return rc;
 }
 
+int validate_linear(const void *x, const void *w, const void *y, int in_dtype, int out_dtype,
+                    int m, int n, int k, int64_t x_rs, int64_t w_rs, int64_t y_rs) {
+  if (in_dtype != WATTN_F16 && in_dtype != WATTN_BF16)
+    return set_error(WATTN_ERR_UNSUPPORTED, "linear: inputs must be f16 or bf16");
+  if (!valid_dtype(out_dtype)) return set_error(WATTN_ERR_INVALID, "linear: bad output dtype");
+  if (m < 0 || n < 0 || k < 1) return set_error(WATTN_ERR_INVALID, "linear: bad sizes");
+  if (x_rs < k || w_rs < k || y_rs < n)
+    return set_error(WATTN_ERR_INVALID, "linear: row stride below the row length");
+  if (m == 0 || n == 0) return WATTN_OK;
+  if (!x || !w || !y) return set_error(WATTN_ERR_INVALID, "linear: NULL tensor");
+  if (((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15) ||
+      ((x_rs * 2) & 15) || ((w_rs * 2) & 15))
+    return set_error(WATTN_ERR_INVALID,
+                     "linear: x and W need 16-byte aligned rows (base and row stride)");
+  return WATTN_OK;
+}
+
+int wattn_linear_fwd(const void *x, const void *w, const float *bias, void *y, int in_dtype,
+                     int out_dtype, int m, int n, int k, int64_t x_row_stride,
+                     int64_t w_row_stride, int64_t y_row_stride, void *stream) {
+  clear_error();
+  int rc = validate_linear(x, w, y, in_dtype, out_dtype, m, n, k, x_row_stride, w_row_stride,
+                           y_row_stride);
+  if (rc != WATTN_OK || m == 0 || n == 0) return rc;
+  return launch_linear(x, w, bias, y, in_dtype, out_dtype, m, n, k, x_row_stride, w_row_stride,
+                       y_row_stride, (cudaStream_t)stream);
+}
+
+int wattn_cross_kv_project(const void *enc, const void *wk, const void *wv, const float *bv,
+                           void *k_out, void *v_out, int in_dtype, int out_dtype, int n_tokens,
+                           int d_model, int64_t enc_row_stride, int64_t kv_row_stride,
+                           void *stream) {
+  clear_error();
+  int rc = validate_linear(enc, wk, k_out, in_dtype, out_dtype, n_tokens, d_model, d_model,
+                           enc_row_stride, d_model, kv_row_stride);
+  if (rc == WATTN_OK)
+    rc = validate_linear(enc, wv, v_out, in_dtype, out_dtype, n_tokens, d_model, d_model,
+                         enc_row_stride, d_model, kv_row_stride);
+  if (rc != WATTN_OK || n_tokens == 0) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  // decoder.rs:433-442: K without bias, V with the value bias.
+  rc = launch_linear(enc, wk, nullptr, k_out, in_dtype, out_dtype, n_tokens, d_model, d_model,
+                     enc_row_stride, d_model, kv_row_stride, st);
+  if (rc != WATTN_OK) return rc;
+  return launch_linear(enc, wv, bv, v_out, in_dtype, out_dtype, n_tokens, d_model, d_model,
+                       enc_row_stride, d_model, kv_row_stride, st);
+}
+
 int wattn_selftest_bounded_wait(int limit_us, void *stream) {
   clear_error();
   if (limit_us <= 0 || limit_us > 2000000)

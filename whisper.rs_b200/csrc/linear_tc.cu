@@ -1,0 +1,244 @@
+// linear_tc.cu -- y = x W^T (+ bias) on the sm_100a tensor cores.
+//
+// The projection of Weight::linear (crates/tensor/src/weight.rs:121,
+// ops/matmul.rs:4-110: output[t][r] = sum_c x[t][c] * W[r][c] + bias[r]) for
+// 16-bit x and W with f32 accumulation. It produces the decoder's
+// cross-attention K and V on the device (precompute_cross_attn,
+// crates/whisper/src/decoder.rs:423-447), straight into the layout the decode
+// kernels read, so the encoder output never leaves the GPU.
+//
+// Both operands are K-major, the layout tcgen05 reads: one CTA computes a
+// 128 x 256 tile of y; a TMA warp streams 64-deep k-tiles of x (128 rows) and
+// W (256 rows) through a 4-stage ring (128-byte swizzle); an MMA warp issues
+// tcgen05.mma M=128, N=256, K=16 (the shape that runs at the tensor-core
+// peak) into 256 TMEM columns; four epilogue warps, one per TMEM lane
+// quarter, add the bias and store their row in the output type. Ragged
+// edges: TMA fills out-of-range rows and k with zeros, the epilogue masks the
+// stores.
+
+#include "wattn_common.cuh"
+#include "wattn_internal.h"
+
+namespace wattn {
+namespace {
+
+constexpr int kLinBM = 128;
+constexpr int kLinBN = 256;
+constexpr int kLinBK = 64;                      // one 128-byte swizzle atom of 16-bit
+constexpr int kLinStages = 4;
+constexpr int kLinABytes = kLinBM * kLinBK * 2;  // 16 KB
+constexpr int kLinBBytes = kLinBN * kLinBK * 2;  // 32 KB
+constexpr int kLinTmaWarp = 0, kLinMmaWarp = 1;
+constexpr int kLinThreads = 6 * 32;              // + four epilogue warps
+constexpr uint32_t kLinTmemCols = 256;
+
+struct LinSmem {
+  uint8_t a[kLinStages][kLinABytes];
+  uint8_t b[kLinStages][kLinBBytes];
+  uint64_t full[kLinStages], empty[kLinStages];
+  uint64_t acc_full;
+  uint32_t tmem_base;
+  int abort;
+};
+
+struct LinParams {
+  void *y;
+  const float *bias;  // f32 [n] or nullptr
+  int64_t y_rs;
+  int m, n, k;
+  int *status;
+};
+
+#define LIN_SITE(role, bar, j) ((3 << 24) | ((role) << 16) | ((bar) << 8) | ((j) & 0xff))
+
+template <int IN_DT, int OUT_DT>
+__global__ void __launch_bounds__(kLinThreads, 1)
+    linear_tc_kernel(const __grid_constant__ CUtensorMap map_x,
+                     const __grid_constant__ CUtensorMap map_w, const LinParams p) {
+  using OutT = typename Elem<OUT_DT>::T;
+  extern __shared__ uint8_t lin_smem_raw[];
+  LinSmem &s = *reinterpret_cast<LinSmem *>(
+      (reinterpret_cast<uintptr_t>(lin_smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * kLinBM, n0 = blockIdx.y * kLinBN;
+  const int nk = (p.k + kLinBK - 1) / kLinBK;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kLinStages; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    mbar_init(&s.acc_full, 1);
+    s.abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == kLinMmaWarp) {
+    __syncwarp();
+    tmem_alloc(&s.tmem_base, kLinTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+  volatile int *abort = &s.abort;
+
+  if (warp == kLinTmaWarp) {
+    if (lane == 0) {
+      tma_prefetch_desc(&map_x);
+      tma_prefetch_desc(&map_w);
+      int last = -1;
+      for (int kt = 0; kt < nk; ++kt) {
+        const int st = kt % kLinStages;
+        const uint32_t ph = (kt / kLinStages) & 1;
+        if (!mbar_wait(&s.empty[st], ph ^ 1, abort, p.status, LIN_SITE(1, 1, kt))) break;
+        mbar_arrive_expect_tx(&s.full[st], kLinABytes + kLinBBytes);
+        tma_load_2d(s.a[st], &map_x, &s.full[st], kt * kLinBK, m0);
+        tma_load_2d(s.b[st], &map_w, &s.full[st], kt * kLinBK, n0);
+        last = kt;
+      }
+      if (*abort && last >= 0) {
+        // Let the loads in flight land before shared memory is released.
+        volatile int no_abort = 0;
+        mbar_wait(&s.full[last % kLinStages], (last / kLinStages) & 1, &no_abort, p.status,
+                  LIN_SITE(1, 2, last));
+      }
+    }
+  } else if (warp == kLinMmaWarp) {
+    if (lane == 0) {
+      constexpr uint32_t ab = IN_DT == WATTN_BF16 ? 1u : 0u;
+      constexpr uint32_t idesc = idesc_f16(ab, kLinBM, kLinBN, 0, 0);
+      const uint32_t a0 = smem_u32(s.a[0]), b0 = smem_u32(s.b[0]);
+      bool ok = true;
+      for (int kt = 0; kt < nk; ++kt) {
+        const int st = kt % kLinStages;
+        const uint32_t ph = (kt / kLinStages) & 1;
+        if (!mbar_wait(&s.full[st], ph, abort, p.status, LIN_SITE(2, 0, kt))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kLinBK / 16; ++kk)
+          umma_ss(tmem, smem_desc_sw128(a0 + st * kLinABytes + kk * 32, 16, 1024),
+                  smem_desc_sw128(b0 + st * kLinBBytes + kk * 32, 16, 1024), idesc,
+                  kt > 0 || kk > 0);
+        umma_commit(&s.empty[st]);
+      }
+      (void)ok;
+      // acc_full also serves as the drain: it completes once every MMA
+      // issued above has.
+      umma_commit(&s.acc_full);
+    }
+  } else {
+    // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. 32 (w % 4) + 31
+    const int q = warp & 3;
+    const int row = m0 + q * 32 + lane;
+    const bool got = mbar_wait(&s.acc_full, 0, abort, p.status, LIN_SITE(3, 0, 0));
+    if (__all_sync(0xffffffffu, got)) {
+      tc_fence_after();
+      const uint32_t t_row = tmem + (uint32_t(q * 32) << 16);
+      OutT *yrow = reinterpret_cast<OutT *>(p.y) + (int64_t)row * p.y_rs;
+#pragma unroll 1
+      for (int ch = 0; ch < kLinBN / 32; ++ch) {
+        uint32_t r[32];
+        tmem_ld32(t_row + ch * 32, r);
+        tmem_wait_ld();
+        reg_fence(r);
+        const int c0 = n0 + ch * 32;
+        if (row < p.m && c0 < p.n) {
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int c = c0 + i;
+            v[i] = __uint_as_float(r[i]) + ((p.bias != nullptr && c < p.n) ? __ldg(p.bias + c) : 0.f);
+          }
+          OutT *dst = yrow + c0;
+          if (c0 + 32 <= p.n && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+            if constexpr (sizeof(OutT) == 4) {
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                reinterpret_cast<float4 *>(dst)[i] =
+                    make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                reinterpret_cast<uint4 *>(dst)[i] = make_uint4(
+                    pack2<OutT>(v[8 * i], v[8 * i + 1]), pack2<OutT>(v[8 * i + 2], v[8 * i + 3]),
+                    pack2<OutT>(v[8 * i + 4], v[8 * i + 5]), pack2<OutT>(v[8 * i + 6], v[8 * i + 7]));
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (c0 + i < p.n) dst[i] = from_f32<OutT>(v[i]);
+          }
+        }
+      }
+    } else {
+      // The accumulator never completed (a wait ran out): make sure no MMA
+      // still writes TMEM before it is freed (bounded, ignores abort).
+      volatile int no_abort = 0;
+      mbar_wait(&s.acc_full, 0, &no_abort, p.status, LIN_SITE(3, 1, 0));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kLinMmaWarp) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, kLinTmemCols);
+  }
+}
+
+template <int IN_DT, int OUT_DT>
+int launch_linear_typed(const CUtensorMap &mx, const CUtensorMap &mw, const LinParams &p,
+                        cudaStream_t stream) {
+  auto kern = linear_tc_kernel<IN_DT, OUT_DT>;
+  const int smem = (int)sizeof(LinSmem) + 1024;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+      cudaSuccess)
+    return check_launch("cudaFuncSetAttribute(linear_tc)");
+  const dim3 grid((p.m + kLinBM - 1) / kLinBM, (p.n + kLinBN - 1) / kLinBN);
+  kern<<<grid, kLinThreads, smem, stream>>>(mx, mw, p);
+  return check_launch("linear_tc");
+}
+
+}  // namespace
+
+int launch_linear(const void *x, const void *w, const float *bias, void *y, int in_dtype,
+                  int out_dtype, int m, int n, int k, int64_t x_rs, int64_t w_rs, int64_t y_rs,
+                  cudaStream_t stream) {
+  if (m == 0 || n == 0) return WATTN_OK;
+  if ((m + kLinBM - 1) / kLinBM > 2147483647 || (n + kLinBN - 1) / kLinBN > 65535)
+    return set_error(WATTN_ERR_INVALID, "linear: %d output columns exceed the grid", n);
+  CUtensorMap mx, mw;
+  const uint64_t dx[2] = {(uint64_t)k, (uint64_t)m}, sx[1] = {(uint64_t)x_rs * 2};
+  const uint64_t dw[2] = {(uint64_t)k, (uint64_t)n}, sw[1] = {(uint64_t)w_rs * 2};
+  const uint32_t bx[2] = {kLinBK, kLinBM}, bw[2] = {kLinBK, kLinBN};
+  int rc = encode_tmap(&mx, tmap_dtype(in_dtype), 2, x, dx, sx, bx, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc != WATTN_OK) return rc;
+  rc = encode_tmap(&mw, tmap_dtype(in_dtype), 2, w, dw, sw, bw, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc != WATTN_OK) return rc;
+  LinParams p;
+  p.y = y;
+  p.bias = bias;
+  p.y_rs = y_rs;
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.status = device_status_ptr();
+  if (p.status == nullptr) return WATTN_ERR_CUDA;
+#define WATTN_LIN_CASE(ID, OD) \
+  if (in_dtype == ID && out_dtype == OD) return launch_linear_typed<ID, OD>(mx, mw, p, stream);
+  WATTN_LIN_CASE(WATTN_F16, WATTN_F32)
+  WATTN_LIN_CASE(WATTN_F16, WATTN_F16)
+  WATTN_LIN_CASE(WATTN_F16, WATTN_BF16)
+  WATTN_LIN_CASE(WATTN_BF16, WATTN_F32)
+  WATTN_LIN_CASE(WATTN_BF16, WATTN_F16)
+  WATTN_LIN_CASE(WATTN_BF16, WATTN_BF16)
+#undef WATTN_LIN_CASE
+  return set_error(WATTN_ERR_INVALID, "linear: 16-bit inputs only");
+}
+
+}  // namespace wattn

@@ -67,6 +67,9 @@ _SIGS = {
     "wattn_decode_fwd_capture": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i,
                                       _i64, _i64, _i64, _i64, _f, _vp, _sz, _ip, _ip, _i, _i, _i,
                                       _vp, _vp]),
+    "wattn_linear_fwd": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i64, _i64, _i64, _vp]),
+    "wattn_cross_kv_project": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i64, _i64,
+                                    _vp]),
     "wattn_kv_create": (_i, [ctypes.POINTER(_vp), _i, _i, _i, _i, _i, _i, _i, _i]),
     "wattn_kv_destroy": (_i, [_vp]),
     "wattn_kv_clear": (_i, [_vp]),
@@ -315,6 +318,26 @@ def decode_fwd_capture(q, k, v, o, *, n_groups, group_size, t_kv, n_heads, scale
                                         ws_ptr, ws_bytes, _iarr(slots), _iarr(heads),
                                         len(selected), n_selected, row_offset, _dev(capture),
                                         _stream_ptr(stream)), "decode_fwd_capture")
+
+
+def linear_fwd(x, w, y, *, m, n, k, bias=None, x_row_stride=None, w_row_stride=None,
+               y_row_stride=None, stream=None) -> None:
+    """``wattn_linear_fwd``: y = x W^T (+ bias) on CUDA tensors (x, W 16-bit of
+    one type, bias f32 or None)."""
+    _check(lib.wattn_linear_fwd(_dev(x), _dev(w), _dev(bias) if bias is not None else None,
+                                _dev(y), _dt_of(x), _dt_of(y), m, n, k, x_row_stride or k,
+                                w_row_stride or k, y_row_stride or n, _stream_ptr(stream)),
+           "linear_fwd")
+
+
+def cross_kv_project(enc, wk, wv, bv, k_out, v_out, *, n_tokens, d_model, enc_row_stride=None,
+                     kv_row_stride=None, stream=None) -> None:
+    """``wattn_cross_kv_project``: one layer of precompute_cross_attn
+    (decoder.rs:423-447) on the device."""
+    _check(lib.wattn_cross_kv_project(_dev(enc), _dev(wk), _dev(wv), _dev(bv), _dev(k_out),
+                                      _dev(v_out), _dt_of(enc), _dt_of(k_out), n_tokens, d_model,
+                                      enc_row_stride or d_model, kv_row_stride or d_model,
+                                      _stream_ptr(stream)), "cross_kv_project")
 
 
 def decode_fwd_noalloc(q, k, v, o, *, n_groups, group_size, t_kv, n_heads, scale,
