@@ -7,17 +7,20 @@
 // crates/whisper/src/decoder.rs:423-447), straight into the layout the decode
 // kernels read, so the encoder output never leaves the GPU.
 //
-// Both operands are K-major, the layout tcgen05 reads: one CTA computes a
-// 128 x 256 tile of y; a TMA warp streams 64-deep k-tiles of x (128 rows) and
-// W (256 rows) through a 4-stage ring (128-byte swizzle); an MMA warp issues
-// tcgen05.mma M=128, N=256, K=16 (the shape that runs at the tensor-core
-// peak) into 256 TMEM columns; four epilogue warps, one per TMEM lane
-// quarter, add the bias and store their row in the output type. Ragged
-// edges: TMA fills out-of-range rows and k with zeros, the epilogue masks the
-// stores.
+// Both operands are K-major, the layout tcgen05 reads. A persistent grid
+// (one CTA per SM) walks 128 x 256 tiles of y: a TMA warp streams 64-deep
+// k-tiles of x (128 rows) and W (256 rows) through a 4-stage ring (128-byte
+// swizzle) without pausing between tiles; an MMA warp issues tcgen05.mma
+// M=128, N=256, K=16 (the shape that runs at the tensor-core peak) into one
+// of two 256-column TMEM accumulators; four epilogue warps, one per TMEM lane
+// quarter, add the bias and store the previous tile from the other
+// accumulator meanwhile. Ragged edges: TMA fills out-of-range rows and k with
+// zeros, the epilogue masks the stores.
 
 #include "wattn_common.cuh"
 #include "wattn_internal.h"
+
+#include <algorithm>
 
 namespace wattn {
 namespace {
@@ -30,13 +33,15 @@ constexpr int kLinABytes = kLinBM * kLinBK * 2;  // 16 KB
 constexpr int kLinBBytes = kLinBN * kLinBK * 2;  // 32 KB
 constexpr int kLinTmaWarp = 0, kLinMmaWarp = 1;
 constexpr int kLinThreads = 6 * 32;              // + four epilogue warps
-constexpr uint32_t kLinTmemCols = 256;
+constexpr uint32_t kLinTmemCols = 512;           // two 256-column accumulators
 
 struct LinSmem {
   uint8_t a[kLinStages][kLinABytes];
   uint8_t b[kLinStages][kLinBBytes];
   uint64_t full[kLinStages], empty[kLinStages];
-  uint64_t acc_full;
+  uint64_t acc_full[2];   // accumulator b holds a finished tile (MMA commit)
+  uint64_t acc_empty[2];  // the epilogue has read accumulator b (one arrival per warp)
+  uint64_t drain;
   uint32_t tmem_base;
   int abort;
 };
@@ -46,6 +51,7 @@ struct LinParams {
   const float *bias;  // f32 [n] or nullptr
   int64_t y_rs;
   int m, n, k;
+  int tiles_n, n_tiles;  // tiles along n; all tiles (row-tile major)
   int *status;
 };
 
@@ -60,7 +66,6 @@ __global__ void __launch_bounds__(kLinThreads, 1)
   LinSmem &s = *reinterpret_cast<LinSmem *>(
       (reinterpret_cast<uintptr_t>(lin_smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * kLinBM, n0 = blockIdx.y * kLinBN;
   const int nk = (p.k + kLinBK - 1) / kLinBK;
 
   if (threadIdx.x == 0) {
@@ -68,7 +73,11 @@ __global__ void __launch_bounds__(kLinThreads, 1)
       mbar_init(&s.full[i], 1);
       mbar_init(&s.empty[i], 1);
     }
-    mbar_init(&s.acc_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s.acc_full[b], 1);
+      mbar_init(&s.acc_empty[b], 4);
+    }
+    mbar_init(&s.drain, 1);
     s.abort = 0;
     fence_barrier_init();
   }
@@ -87,15 +96,23 @@ __global__ void __launch_bounds__(kLinThreads, 1)
     if (lane == 0) {
       tma_prefetch_desc(&map_x);
       tma_prefetch_desc(&map_w);
+      uint32_t c = 0;  // ring position over all tiles of this CTA
       int last = -1;
-      for (int kt = 0; kt < nk; ++kt) {
-        const int st = kt % kLinStages;
-        const uint32_t ph = (kt / kLinStages) & 1;
-        if (!mbar_wait(&s.empty[st], ph ^ 1, abort, p.status, LIN_SITE(1, 1, kt))) break;
-        mbar_arrive_expect_tx(&s.full[st], kLinABytes + kLinBBytes);
-        tma_load_2d(s.a[st], &map_x, &s.full[st], kt * kLinBK, m0);
-        tma_load_2d(s.b[st], &map_w, &s.full[st], kt * kLinBK, n0);
-        last = kt;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < p.n_tiles; t += gridDim.x) {
+        const int m0 = (t / p.tiles_n) * kLinBM, n0 = (t % p.tiles_n) * kLinBN;
+        for (int kt = 0; kt < nk; ++kt, ++c) {
+          const int st = c % kLinStages;
+          const uint32_t ph = (c / kLinStages) & 1;
+          if (!mbar_wait(&s.empty[st], ph ^ 1, abort, p.status, LIN_SITE(1, 1, kt))) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&s.full[st], kLinABytes + kLinBBytes);
+          tma_load_2d(s.a[st], &map_x, &s.full[st], kt * kLinBK, m0);
+          tma_load_2d(s.b[st], &map_w, &s.full[st], kt * kLinBK, n0);
+          last = (int)c;
+        }
       }
       if (*abort && last >= 0) {
         // Let the loads in flight land before shared memory is released.
@@ -109,35 +126,53 @@ __global__ void __launch_bounds__(kLinThreads, 1)
       constexpr uint32_t ab = IN_DT == WATTN_BF16 ? 1u : 0u;
       constexpr uint32_t idesc = idesc_f16(ab, kLinBM, kLinBN, 0, 0);
       const uint32_t a0 = smem_u32(s.a[0]), b0 = smem_u32(s.b[0]);
+      uint32_t c = 0;
+      int i = 0;  // tiles of this CTA so far
       bool ok = true;
-      for (int kt = 0; kt < nk; ++kt) {
-        const int st = kt % kLinStages;
-        const uint32_t ph = (kt / kLinStages) & 1;
-        if (!mbar_wait(&s.full[st], ph, abort, p.status, LIN_SITE(2, 0, kt))) {
-          ok = false;
+      for (int t = blockIdx.x; ok && t < p.n_tiles; t += gridDim.x, ++i) {
+        const int b = i & 1;
+        // Accumulator b was last used by tile i - 2: its epilogue must be done.
+        if (i >= 2 && !mbar_wait(&s.acc_empty[b], ((i >> 1) + 1) & 1, abort, p.status,
+                                 LIN_SITE(2, 1, i)))
           break;
-        }
         tc_fence_after();
+        const uint32_t acc = tmem + b * 256;
+        for (int kt = 0; kt < nk; ++kt, ++c) {
+          const int st = c % kLinStages;
+          const uint32_t ph = (c / kLinStages) & 1;
+          if (!mbar_wait(&s.full[st], ph, abort, p.status, LIN_SITE(2, 0, kt))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < kLinBK / 16; ++kk)
-          umma_ss(tmem, smem_desc_sw128(a0 + st * kLinABytes + kk * 32, 16, 1024),
-                  smem_desc_sw128(b0 + st * kLinBBytes + kk * 32, 16, 1024), idesc,
-                  kt > 0 || kk > 0);
-        umma_commit(&s.empty[st]);
+          for (int kk = 0; kk < kLinBK / 16; ++kk)
+            umma_ss(acc, smem_desc_sw128(a0 + st * kLinABytes + kk * 32, 16, 1024),
+                    smem_desc_sw128(b0 + st * kLinBBytes + kk * 32, 16, 1024), idesc,
+                    kt > 0 || kk > 0);
+          umma_commit(&s.empty[st]);
+        }
+        if (!ok) break;
+        umma_commit(&s.acc_full[b]);
       }
-      (void)ok;
-      // acc_full also serves as the drain: it completes once every MMA
-      // issued above has.
-      umma_commit(&s.acc_full);
+      // Drain: every MMA issued above completes before TMEM is freed
+      // (bounded, ignores abort).
+      volatile int no_abort = 0;
+      umma_commit(&s.drain);
+      mbar_wait(&s.drain, 0, &no_abort, p.status, LIN_SITE(2, 2, 0));
     }
   } else {
     // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. 32 (w % 4) + 31
     const int q = warp & 3;
-    const int row = m0 + q * 32 + lane;
-    const bool got = mbar_wait(&s.acc_full, 0, abort, p.status, LIN_SITE(3, 0, 0));
-    if (__all_sync(0xffffffffu, got)) {
+    int i = 0;
+    for (int t = blockIdx.x; t < p.n_tiles; t += gridDim.x, ++i) {
+      const int b = i & 1;
+      const int m0 = (t / p.tiles_n) * kLinBM, n0 = (t % p.tiles_n) * kLinBN;
+      const bool got = mbar_wait(&s.acc_full[b], (i >> 1) & 1, abort, p.status, LIN_SITE(3, 0, i));
+      if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
-      const uint32_t t_row = tmem + (uint32_t(q * 32) << 16);
+      const int row = m0 + q * 32 + lane;
+      const uint32_t t_row = tmem + b * 256 + (uint32_t(q * 32) << 16);
       OutT *yrow = reinterpret_cast<OutT *>(p.y) + (int64_t)row * p.y_rs;
 #pragma unroll 1
       for (int ch = 0; ch < kLinBN / 32; ++ch) {
@@ -149,36 +184,37 @@ __global__ void __launch_bounds__(kLinThreads, 1)
         if (row < p.m && c0 < p.n) {
           float v[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int c = c0 + i;
-            v[i] = __uint_as_float(r[i]) + ((p.bias != nullptr && c < p.n) ? __ldg(p.bias + c) : 0.f);
+          for (int e = 0; e < 32; ++e) {
+            const int col = c0 + e;
+            v[e] = __uint_as_float(r[e]) +
+                   ((p.bias != nullptr && col < p.n) ? __ldg(p.bias + col) : 0.f);
           }
           OutT *dst = yrow + c0;
           if (c0 + 32 <= p.n && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
             if constexpr (sizeof(OutT) == 4) {
 #pragma unroll
-              for (int i = 0; i < 8; ++i)
-                reinterpret_cast<float4 *>(dst)[i] =
-                    make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+              for (int e = 0; e < 8; ++e)
+                reinterpret_cast<float4 *>(dst)[e] =
+                    make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
             } else {
 #pragma unroll
-              for (int i = 0; i < 4; ++i)
-                reinterpret_cast<uint4 *>(dst)[i] = make_uint4(
-                    pack2<OutT>(v[8 * i], v[8 * i + 1]), pack2<OutT>(v[8 * i + 2], v[8 * i + 3]),
-                    pack2<OutT>(v[8 * i + 4], v[8 * i + 5]), pack2<OutT>(v[8 * i + 6], v[8 * i + 7]));
+              for (int e = 0; e < 4; ++e)
+                reinterpret_cast<uint4 *>(dst)[e] = make_uint4(
+                    pack2<OutT>(v[8 * e], v[8 * e + 1]), pack2<OutT>(v[8 * e + 2], v[8 * e + 3]),
+                    pack2<OutT>(v[8 * e + 4], v[8 * e + 5]),
+                    pack2<OutT>(v[8 * e + 6], v[8 * e + 7]));
             }
           } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (c0 + i < p.n) dst[i] = from_f32<OutT>(v[i]);
+            for (int e = 0; e < 32; ++e)
+              if (c0 + e < p.n) dst[e] = from_f32<OutT>(v[e]);
           }
         }
       }
-    } else {
-      // The accumulator never completed (a wait ran out): make sure no MMA
-      // still writes TMEM before it is freed (bounded, ignores abort).
-      volatile int no_abort = 0;
-      mbar_wait(&s.acc_full, 0, &no_abort, p.status, LIN_SITE(3, 1, 0));
+      // Accumulator b may take the tile after next.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.acc_empty[b]);
     }
   }
 
@@ -199,8 +235,12 @@ int launch_linear_typed(const CUtensorMap &mx, const CUtensorMap &mw, const LinP
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
       cudaSuccess)
     return check_launch("cudaFuncSetAttribute(linear_tc)");
-  const dim3 grid((p.m + kLinBM - 1) / kLinBM, (p.n + kLinBN - 1) / kLinBN);
-  kern<<<grid, kLinThreads, smem, stream>>>(mx, mw, p);
+  // Persistent grid: one CTA per SM (the ring's shared memory allows no second).
+  int dev = 0, n_sm = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return check_launch("linear_tc: device query");
+  kern<<<std::min(p.n_tiles, n_sm), kLinThreads, smem, stream>>>(mx, mw, p);
   return check_launch("linear_tc");
 }
 
@@ -210,8 +250,9 @@ int launch_linear(const void *x, const void *w, const float *bias, void *y, int 
                   int out_dtype, int m, int n, int k, int64_t x_rs, int64_t w_rs, int64_t y_rs,
                   cudaStream_t stream) {
   if (m == 0 || n == 0) return WATTN_OK;
-  if ((m + kLinBM - 1) / kLinBM > 2147483647 || (n + kLinBN - 1) / kLinBN > 65535)
-    return set_error(WATTN_ERR_INVALID, "linear: %d output columns exceed the grid", n);
+  const long long tiles_m = (m + kLinBM - 1) / kLinBM, tiles_n = (n + kLinBN - 1) / kLinBN;
+  if (tiles_m * tiles_n > 2147483647LL)
+    return set_error(WATTN_ERR_INVALID, "linear: %lld tiles exceed 2^31", tiles_m * tiles_n);
   CUtensorMap mx, mw;
   const uint64_t dx[2] = {(uint64_t)k, (uint64_t)m}, sx[1] = {(uint64_t)x_rs * 2};
   const uint64_t dw[2] = {(uint64_t)k, (uint64_t)n}, sw[1] = {(uint64_t)w_rs * 2};
@@ -227,6 +268,8 @@ int launch_linear(const void *x, const void *w, const float *bias, void *y, int 
   p.m = m;
   p.n = n;
   p.k = k;
+  p.tiles_n = (int)tiles_n;
+  p.n_tiles = (int)(tiles_m * tiles_n);
   p.status = device_status_ptr();
   if (p.status == nullptr) return WATTN_ERR_CUDA;
 #define WATTN_LIN_CASE(ID, OD) \
