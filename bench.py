@@ -396,6 +396,48 @@ def bench_turbo_decode(W, rank, world, steps, warmup):
             "mean_cache_len": float(lens.mean())}
 
 
+# --------------------------------------------------------------------- cross K/V projection (rank 0)
+
+def bench_cross_kv_projection(W, steps: int, warmup: int):
+    """precompute_cross_attn (decoder.rs:423-447) on the device for config 4's
+    32 utterances at once: K = enc Wk^T, V = enc Wv^T + bv for one large-v3
+    layer (48000 x 1280 x 1280 bf16 GEMMs, f16 output in the decode layout)."""
+    import torch
+    n_tok, d = C4["utterances"] * C4["t_audio"], C4["heads"] * 64
+    g = torch.Generator(device="cuda").manual_seed(31)
+    sets = []
+    for r in range(2):  # two layers' inputs cycled (each > L2)
+        enc = torch.randn(n_tok * d, generator=g, device="cuda").to(torch.bfloat16)
+        wk = (torch.randn(d * d, generator=g, device="cuda") * 0.03).to(torch.bfloat16)
+        wv = (torch.randn(d * d, generator=g, device="cuda") * 0.03).to(torch.bfloat16)
+        bv = torch.randn(d, generator=g, device="cuda")
+        sets.append((enc, wk, wv, bv))
+    k_out = torch.empty(n_tok * d, dtype=torch.float16, device="cuda")
+    v_out = torch.empty_like(k_out)
+    stream = torch.cuda.current_stream()
+
+    def run(i):
+        enc, wk, wv, bv = sets[i % 2]
+        W.cross_kv_project(enc, wk, wv, bv, k_out, v_out, n_tokens=n_tok, d_model=d,
+                           stream=stream)
+
+    for i in range(max(warmup, 3)):
+        run(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        run(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    flops = 2 * 2 * n_tok * d * d
+    del sets
+    return {"config": "c4_cross_kv_projection_layer", "value": flops / (ms * 1e-3) / 1e12,
+            "unit": "TFLOP/s", "ms_per_layer": ms, "kernel": "linear_tc",
+            "launches_per_layer": 2, "l2": "inputs 123 MB > L2, two input sets cycled"}
+
+
 # --------------------------------------------------------------------- small configs (rank 0)
 
 def bench_small(W, cfg: str, steps: int, warmup: int):
@@ -532,7 +574,8 @@ def main():
         dec = bench_turbo_decode(W, rank, world, max(5, a.steps), warmup)
         xdec = bench_cross_decode(W, rank, world, max(2, a.steps // 3), warmup)
         if rank == 0:
-            also = [bench_small(W, "c2", 20, warmup), bench_small(W, "c1", 20, warmup)]
+            also = [bench_small(W, "c2", 20, warmup), bench_small(W, "c1", 20, warmup),
+                    bench_cross_kv_projection(W, 20, warmup)]
     cb = cpu_baseline(a.cpu_seconds) if (rank == 0 and world == 1 and a.cpu_seconds > 0) else None
     if world > 1:
         import torch.distributed as dist
