@@ -438,6 +438,48 @@ def bench_cross_kv_projection(W, steps: int, warmup: int):
             "launches_per_layer": 2, "l2": "inputs 123 MB > L2, two input sets cycled"}
 
 
+def bench_encoder_block(W, steps: int, warmup: int):
+    """Config 3's encoder attention sub-block (encoder.rs:276-303) for one
+    layer: QKV projection (48000 x 3840 x 1280), attention over the fused rows
+    in place, output projection (48000 x 1280 x 1280), bf16 in, bf16 out."""
+    import torch
+    b, t, h = C3["batch"], C3["t"], C3["heads"]
+    d, rows = h * 64, C3["batch"] * C3["t"]
+    g = torch.Generator(device="cuda").manual_seed(41)
+    s = d ** -0.5
+    x = torch.randn(rows * d, generator=g, device="cuda").to(torch.bfloat16)
+    wq = (torch.randn(3 * d * d, generator=g, device="cuda") * s).to(torch.bfloat16)
+    wo = (torch.randn(d * d, generator=g, device="cuda") * s).to(torch.bfloat16)
+    bq = torch.randn(3 * d, generator=g, device="cuda") * 0.1
+    bo = torch.randn(d, generator=g, device="cuda") * 0.1
+    y = torch.empty(rows * d, dtype=torch.bfloat16, device="cuda")
+    ws = torch.empty(W.encoder_attention_workspace_bytes(b, t, h), dtype=torch.uint8,
+                     device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def run():
+        W.encoder_attention(x, wq, bq, wo, bo, y, batch=b, t=t, n_heads=h, workspace=ws,
+                            stream=stream)
+
+    for _ in range(max(warmup, 3)):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        run()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    flops = 2 * rows * 3 * d * d + enc_flops(b, h, t, t) + 2 * rows * d * d
+    del x, wq, wo, y, ws
+    torch.cuda.empty_cache()
+    return {"config": "c3_encoder_attention_block_layer", "value": flops / (ms * 1e-3) / 1e12,
+            "unit": "TFLOP/s", "ms_per_layer": ms,
+            "kernels": ["linear_tc (QKV)", "attn_fwd_tc", "linear_tc (out)"],
+            "l2": "inputs exceed L2 (x 123 MB, QKV 369 MB)"}
+
+
 # --------------------------------------------------------------------- small configs (rank 0)
 
 def bench_small(W, cfg: str, steps: int, warmup: int):
@@ -575,7 +617,7 @@ def main():
         xdec = bench_cross_decode(W, rank, world, max(2, a.steps // 3), warmup)
         if rank == 0:
             also = [bench_small(W, "c2", 20, warmup), bench_small(W, "c1", 20, warmup),
-                    bench_cross_kv_projection(W, 20, warmup)]
+                    bench_cross_kv_projection(W, 20, warmup), bench_encoder_block(W, 10, warmup)]
     cb = cpu_baseline(a.cpu_seconds) if (rank == 0 and world == 1 and a.cpu_seconds > 0) else None
     if world > 1:
         import torch.distributed as dist

@@ -174,6 +174,21 @@ int wattn_cross_kv_project(const void *enc, const void *wk, const void *wv,
                            int64_t enc_row_stride, int64_t kv_row_stride,
                            void *stream);
 
+/* The attention sub-block of an encoder layer (crates/whisper/src/encoder.rs:
+ * 276-303) after its pre-LN: qkv = x W_qkv^T + b_qkv (W_qkv [3d][d]), the
+ * non-causal attention of each utterance's T rows over q, k, v read in place
+ * from the fused [T][3d] rows (the reference splits them into three copies,
+ * :281-286), then y = attn W_out^T + b_out. x [batch*t][d] and the weights
+ * in in_dtype (f16/bf16), biases device f32, y in out_dtype; d = n_heads*64.
+ * The residual add (:304) stays with the caller. workspace: device, 256-byte
+ * aligned, at least wattn_encoder_attention_workspace_bytes() bytes. */
+size_t wattn_encoder_attention_workspace_bytes(int batch, int t, int n_heads);
+int wattn_encoder_attention(const void *x, const void *w_qkv, const float *b_qkv,
+                            const void *w_out, const float *b_out, void *y,
+                            int in_dtype, int out_dtype, int batch, int t,
+                            int n_heads, void *workspace, size_t workspace_bytes,
+                            void *stream);
+
 /* Decode without any allocation. This entry point has no counterpart in the
  * reference: it exists for callers that may not allocate device memory at
  * all (a real-time audio callback, a host whose allocator is frozen after

@@ -815,6 +815,51 @@ int wattn_cross_kv_project(const void *enc, const void *wk, const void *wv, cons
                        enc_row_stride, d_model, kv_row_stride, st);
 }
 
+size_t wattn_encoder_attention_workspace_bytes(int batch, int t, int n_heads) {
+  if (batch <= 0 || t <= 0 || n_heads <= 0) return 0;
+  const size_t rows = (size_t)batch * t, d = (size_t)n_heads * kHeadDim;
+  // fused QKV [rows][3d] then the attention output [rows][d], 16-bit each
+  return round_up(rows * 3 * d * 2, 256) + round_up(rows * d * 2, 256);
+}
+
+int wattn_encoder_attention(const void *x, const void *w_qkv, const float *b_qkv,
+                            const void *w_out, const float *b_out, void *y, int in_dtype,
+                            int out_dtype, int batch, int t, int n_heads, void *workspace,
+                            size_t workspace_bytes, void *stream) {
+  clear_error();
+  if (batch < 0 || t < 0 || n_heads <= 0)
+    return set_error(WATTN_ERR_INVALID, "encoder_attention: bad sizes");
+  if (batch == 0 || t == 0) return WATTN_OK;
+  const int d = n_heads * kHeadDim;
+  const long long rows_ll = (long long)batch * t;
+  if (rows_ll > INT32_MAX) return set_error(WATTN_ERR_INVALID, "encoder_attention: too many rows");
+  const int rows = (int)rows_ll;
+  // (the QKV projection writes the workspace, [rows][3d]; the attention
+  // output, also in the workspace, feeds the output projection)
+  int rc = validate_linear(x, w_qkv, y, in_dtype, in_dtype, rows, 3 * d, d, d, d, 3 * d);
+  if (rc == WATTN_OK) rc = validate_linear(x, w_out, y, in_dtype, out_dtype, rows, d, d, d, d, d);
+  if (rc != WATTN_OK) return rc;
+  const size_t need = wattn_encoder_attention_workspace_bytes(batch, t, n_heads);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255))
+    return set_error(WATTN_ERR_INVALID,
+                     "encoder_attention: a 256-byte aligned workspace of %zu bytes is needed", need);
+  cudaStream_t st = (cudaStream_t)stream;
+  uint8_t *qkv = reinterpret_cast<uint8_t *>(workspace);
+  uint8_t *attn = qkv + round_up((size_t)rows * 3 * d * 2, 256);
+  // encoder.rs:276-279: the fused projection, [rows][q | k | v]
+  rc = launch_linear(x, w_qkv, b_qkv, qkv, in_dtype, in_dtype, rows, 3 * d, d, d, d, 3 * d, st);
+  if (rc != WATTN_OK) return rc;
+  // encoder.rs:281-299: attention reads q, k, v in place (row stride 3d),
+  // without the split copy; scale 1/sqrt(64) as flash_attention_2 uses
+  const int64_t qkv_bs = (int64_t)t * 3 * d;
+  rc = attention_device(qkv, qkv + (size_t)d * 2, qkv + (size_t)2 * d * 2, attn, in_dtype,
+                        in_dtype, batch, t, t, n_heads, 3 * d, 3 * d, d, qkv_bs, qkv_bs,
+                        (int64_t)t * d, 0.125f, 0, 0, st);
+  if (rc != WATTN_OK) return rc;
+  // encoder.rs:301-303: output projection
+  return launch_linear(attn, w_out, b_out, y, in_dtype, out_dtype, rows, d, d, d, d, d, st);
+}
+
 int wattn_selftest_bounded_wait(int limit_us, void *stream) {
   clear_error();
   if (limit_us <= 0 || limit_us > 2000000)

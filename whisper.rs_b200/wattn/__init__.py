@@ -70,6 +70,9 @@ _SIGS = {
     "wattn_linear_fwd": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i64, _i64, _i64, _vp]),
     "wattn_cross_kv_project": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i64, _i64,
                                     _vp]),
+    "wattn_encoder_attention_workspace_bytes": (_sz, [_i, _i, _i]),
+    "wattn_encoder_attention": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz,
+                                     _vp]),
     "wattn_kv_create": (_i, [ctypes.POINTER(_vp), _i, _i, _i, _i, _i, _i, _i, _i]),
     "wattn_kv_destroy": (_i, [_vp]),
     "wattn_kv_clear": (_i, [_vp]),
@@ -338,6 +341,21 @@ def cross_kv_project(enc, wk, wv, bv, k_out, v_out, *, n_tokens, d_model, enc_ro
                                       _dev(v_out), _dt_of(enc), _dt_of(k_out), n_tokens, d_model,
                                       enc_row_stride or d_model, kv_row_stride or d_model,
                                       _stream_ptr(stream)), "cross_kv_project")
+
+
+def encoder_attention_workspace_bytes(batch, t, n_heads) -> int:
+    return lib.wattn_encoder_attention_workspace_bytes(batch, t, n_heads)
+
+
+def encoder_attention(x, w_qkv, b_qkv, w_out, b_out, y, *, batch, t, n_heads, workspace,
+                      stream=None) -> None:
+    """``wattn_encoder_attention``: QKV projection, attention over the fused
+    rows and output projection of an encoder layer (encoder.rs:276-303)."""
+    _check(lib.wattn_encoder_attention(_dev(x), _dev(w_qkv), _dev(b_qkv), _dev(w_out),
+                                       _dev(b_out), _dev(y), _dt_of(x), _dt_of(y), batch, t,
+                                       n_heads, _dev(workspace),
+                                       workspace.numel() * workspace.element_size(),
+                                       _stream_ptr(stream)), "encoder_attention")
 
 
 def decode_fwd_noalloc(q, k, v, o, *, n_groups, group_size, t_kv, n_heads, scale,
