@@ -564,7 +564,7 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=1)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-extras", action="store_true", help="headline only")
-    ap.add_argument("--only", choices=["all", "enc", "dec", "xdec"], default="all",
+    ap.add_argument("--only", choices=["all", "enc", "dec", "xdec", "proj", "block"], default="all",
                     help="profiling aid: run one workload only")
     ap.add_argument("--layers", type=int, default=None,
                     help="profiling aid: layers of the workload --only selects (config 3 by default)")
@@ -606,6 +606,12 @@ def main():
         return
     if a.only == "xdec":
         print(json.dumps({"cross_decode_only": bench_cross_decode(W, rank, world, a.steps, warmup)}))
+        return
+    if a.only == "proj":
+        print(json.dumps({"cross_kv_projection_only": bench_cross_kv_projection(W, a.steps, warmup)}))
+        return
+    if a.only == "block":
+        print(json.dumps({"encoder_block_only": bench_encoder_block(W, a.steps, warmup)}))
         return
     enc = bench_encoder(W, rank, world, a.steps, warmup, a.e2e_steps)
     peaks = load_peaks()
