@@ -189,6 +189,18 @@ int wattn_encoder_attention(const void *x, const void *w_qkv, const float *b_qkv
                             int n_heads, void *workspace, size_t workspace_bytes,
                             void *stream);
 
+/* The whole attention sub-block of an encoder layer, steps (a)-(d) of
+ * crates/whisper/src/encoder.rs:266-304, in place on the f32 residual stream
+ * x [batch*t][d]: x += out_proj(attention(qkv_proj(layer_norm(x)))), with
+ * layer_norm(eps 1e-5, ln_w / ln_b f32, crates/tensor/src/ops/norm.rs:116)
+ * rounded to `dtype` (f16/bf16) for the projections, the weights in dtype,
+ * the biases f32. Same workspace as wattn_encoder_attention. */
+int wattn_encoder_attention_residual(float *x, const float *ln_w, const float *ln_b,
+                                     const void *w_qkv, const float *b_qkv,
+                                     const void *w_out, const float *b_out, int dtype,
+                                     int batch, int t, int n_heads, void *workspace,
+                                     size_t workspace_bytes, void *stream);
+
 /* Decode without any allocation. This entry point has no counterpart in the
  * reference: it exists for callers that may not allocate device memory at
  * all (a real-time audio callback, a host whose allocator is frozen after

@@ -50,6 +50,7 @@ def lib():
         L.ora_single_token_mha_d64_scalar.argtypes = [_f32p, _f32p, _f32p, _sz, _sz, _sz, _f32p]
         L.ora_mha_with_cache.argtypes = [_f32p, _f32p, _f32p, _sz, _sz, _sz, _sz, _sz, _f32p]
         L.ora_linear.argtypes = [_f32p, _f32p, _f32p, _sz, _sz, _sz, _f32p, ctypes.c_int]
+        L.ora_layer_norm.argtypes = [_f32p, _f32p, _f32p, ctypes.c_float, _sz, _sz, _f32p]
         _i32p = ctypes.POINTER(ctypes.c_int)
         L.ora_capture_heads.argtypes = [_f32p, _f32p, _sz, _sz, _sz, _sz, _i32p, _i32p, _sz, _sz,
                                         _sz, _f32p]
@@ -106,6 +107,14 @@ def single_token_mha_d64(q, k, v, t_kv, n_heads, d_model, scalar=False):
     fn = lib().ora_single_token_mha_d64_scalar if scalar else lib().ora_single_token_mha_d64
     _check(fn(_p(q), _p(k), _p(v), t_kv, n_heads, d_model, _p(out)), "single_token_mha_d64")
     return out
+
+
+def layer_norm(x, gamma, beta, rows, d, eps=1e-5):
+    """crates/tensor/src/ops/norm.rs:116-142."""
+    x, g, b = _f32(x), _f32(gamma), _f32(beta)
+    y = np.empty(rows * d, np.float32)
+    _check(lib().ora_layer_norm(_p(x), _p(g), _p(b), eps, rows, d, _p(y)), "layer_norm")
+    return y
 
 
 def linear(x, w, bias, m, n, k, n_threads=None):

@@ -514,6 +514,27 @@ int ora_linear(const float *x, const float *w, const float *bias, size_t m, size
   return 0;
 }
 
+/* crates/tensor/src/ops/norm.rs:67-98 (layer_norm_row_scalar) over
+ * num_tokens rows (:116-142): mean, population variance, then
+ * (x - mean) / sqrt(var + eps) * gamma + beta. */
+int ora_layer_norm(const float *x, const float *gamma, const float *beta, float eps, size_t rows,
+                   size_t d, float *y) {
+  for (size_t r = 0; r < rows; r++) {
+    const float *xr = x + r * d;
+    float sum = 0.f;
+    for (size_t i = 0; i < d; i++) sum += xr[i];
+    float mean = sum / (float)d;
+    float sq = 0.f;
+    for (size_t i = 0; i < d; i++) {
+      float t = xr[i] - mean;
+      sq += t * t;
+    }
+    float inv_std = 1.0f / sqrtf(sq / (float)d + eps);
+    for (size_t i = 0; i < d; i++) y[r * d + i] = (xr[i] - mean) * inv_std * gamma[i] + beta[i];
+  }
+  return 0;
+}
+
 /* ------------------------------------------- alignment-head capture */
 
 /* crates/whisper/src/decoder.rs:796-828 (capture_cross_attention_heads): for

@@ -17,6 +17,7 @@
  *   ora_mha_with_cache           crates/whisper/src/decoder.rs:835-892
  *   ora_capture_heads            crates/whisper/src/decoder.rs:796-828
  *   ora_linear                   crates/tensor/src/ops/matmul.rs:4-110
+ *   ora_layer_norm               crates/tensor/src/ops/norm.rs:67-142
  *   ora_materialized             crates/tensor/tests/test_flash_attention_tiled.rs:41-89
  *   ora_xorshift_fill            crates/tensor/tests/test_flash_attention_tiled.rs:15-35
  *
@@ -56,6 +57,9 @@ int ora_single_token_mha_d64_scalar(const float *q, const float *k,
 int ora_mha_with_cache(const float *q, const float *k, const float *v,
                        size_t n_tokens, size_t total_tokens, size_t t_past,
                        size_t n_heads, size_t d_model, float *out);
+
+int ora_layer_norm(const float *x, const float *gamma, const float *beta, float eps, size_t rows,
+                   size_t d, float *y);
 
 int ora_linear(const float *x, const float *w, const float *bias, size_t m, size_t n, size_t k,
                float *y, int n_threads);

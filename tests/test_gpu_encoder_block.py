@@ -69,6 +69,55 @@ def test_encoder_attention_block(W, oracle, dt, shape):
     assert float(np.dot(got, y_f) / (np.linalg.norm(got) * np.linalg.norm(y_f))) > 0.9999
 
 
+@pytest.mark.parametrize("dt", [2, 1], ids=["bf16", "f16"])
+@pytest.mark.parametrize("shape", [(2, 300, 6), (3, 129, 2)], ids=["base_like", "ragged"])
+def test_encoder_attention_residual(W, oracle, dt, shape):
+    """Steps (a)-(d) of encoder.rs:266-304 in place on the f32 residual
+    stream: layer norm, projections, attention and residual add; each stage
+    checked on the device's own intermediates (read back from the
+    workspace), as above."""
+    import torch
+    b, t, h = shape
+    d = h * 64
+    rows = b * t
+    s = 1.0 / np.sqrt(d)
+    x0 = randn(10, rows * d) * 2.0 + 0.5
+    ln_w, ln_b = 1.0 + 0.1 * randn(11, d), 0.1 * randn(12, d)
+    wqkv_d, wqkv_f = rounded(randn(13, 3 * d * d) * s, dt)
+    wo_d, wo_f = rounded(randn(14, d * d) * s, dt)
+    bqkv, bo = randn(15, 3 * d) * 0.1, randn(16, d) * 0.1
+    x = torch.from_numpy(x0.copy()).cuda()
+    ws = torch.empty(W.encoder_attention_workspace_bytes(b, t, h), dtype=torch.uint8, device="cuda")
+    cuda = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
+    W.encoder_attention_residual(x, cuda(ln_w), cuda(ln_b), wqkv_d, cuda(bqkv), wo_d, cuda(bo),
+                                 batch=b, t=t, n_heads=h, workspace=ws)
+    torch.cuda.synchronize()
+    tdt = {1: torch.float16, 2: torch.bfloat16}[dt]
+    r256 = lambda n: ((n + 255) // 256) * 256  # noqa: E731
+    o_qkv, o_attn, o_xn = 0, r256(rows * 3 * d * 2), r256(rows * 3 * d * 2) + r256(rows * d * 2)
+    xn_dev = ws[o_xn:o_xn + rows * d * 2].view(tdt).float().cpu().numpy()
+    qkv_dev = ws[o_qkv:o_qkv + rows * 3 * d * 2].view(tdt).float().cpu().numpy()
+    attn_dev = ws[o_attn:o_attn + rows * d * 2].view(tdt).float().cpu().numpy()
+    # (a) layer norm, stored 16-bit: within f32 rounding plus the storage rounding
+    xn_ref = oracle.layer_norm(x0, ln_w, ln_b, rows, d)
+    assert (np.abs(xn_dev - xn_ref) <= 1e-5 * np.abs(xn_ref).max() + half_ulp(xn_ref, dt)).all()
+    # (b) QKV projection of the stored normalised rows
+    qkv_ref = oracle.linear(xn_dev, wqkv_f, bqkv, rows, 3 * d, d)
+    assert (np.abs(qkv_dev - qkv_ref) <= 2e-5 * np.abs(qkv_ref).max() + half_ulp(qkv_ref, dt)
+            + 1e-6).all()
+    # (c) attention over the stored QKV rows
+    qkv3 = qkv_dev.reshape(b, t, 3 * d)
+    attn_ref = np.empty((b, t, d), np.float32)
+    for u in range(b):
+        q, k, v = (np.ascontiguousarray(qkv3[u, :, i * d:(i + 1) * d]) for i in range(3))
+        attn_ref[u] = oracle.flash_attention_2(q, k, v, t, t, h, d, False).reshape(t, d)
+    check_16bit(attn_dev, attn_ref.ravel(), f"attention {shape}", dt)
+    # (d) output projection plus the residual, f32 in place
+    y_ref = x0 + oracle.linear(attn_dev, wo_f, bo, rows, d, d)
+    got = x.cpu().numpy()
+    assert (np.abs(got - y_ref) <= 2e-5 * np.abs(y_ref).max() + 1e-6).all()
+
+
 def test_encoder_attention_rejects_a_small_workspace(W):
     import torch
     b, t, h = 1, 64, 2

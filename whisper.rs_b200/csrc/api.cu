@@ -818,15 +818,29 @@ int wattn_cross_kv_project(const void *enc, const void *wk, const void *wv, cons
 size_t wattn_encoder_attention_workspace_bytes(int batch, int t, int n_heads) {
   if (batch <= 0 || t <= 0 || n_heads <= 0) return 0;
   const size_t rows = (size_t)batch * t, d = (size_t)n_heads * kHeadDim;
-  // fused QKV [rows][3d] then the attention output [rows][d], 16-bit each
-  return round_up(rows * 3 * d * 2, 256) + round_up(rows * d * 2, 256);
+  // fused QKV [rows][3d], the attention output [rows][d] and (for the
+  // residual form) the normalised rows [rows][d], 16-bit each
+  return round_up(rows * 3 * d * 2, 256) + 2 * round_up(rows * d * 2, 256);
 }
+
+static int encoder_attention_impl(const void *x, const void *w_qkv, const float *b_qkv,
+                                  const void *w_out, const float *b_out, void *y, int in_dtype,
+                                  int out_dtype, int batch, int t, int n_heads, void *workspace,
+                                  size_t workspace_bytes, void *stream, bool add_residual);
 
 int wattn_encoder_attention(const void *x, const void *w_qkv, const float *b_qkv,
                             const void *w_out, const float *b_out, void *y, int in_dtype,
                             int out_dtype, int batch, int t, int n_heads, void *workspace,
                             size_t workspace_bytes, void *stream) {
   clear_error();
+  return encoder_attention_impl(x, w_qkv, b_qkv, w_out, b_out, y, in_dtype, out_dtype, batch, t,
+                                n_heads, workspace, workspace_bytes, stream, false);
+}
+
+static int encoder_attention_impl(const void *x, const void *w_qkv, const float *b_qkv,
+                                  const void *w_out, const float *b_out, void *y, int in_dtype,
+                                  int out_dtype, int batch, int t, int n_heads, void *workspace,
+                                  size_t workspace_bytes, void *stream, bool add_residual) {
   if (batch < 0 || t < 0 || n_heads <= 0)
     return set_error(WATTN_ERR_INVALID, "encoder_attention: bad sizes");
   if (batch == 0 || t == 0) return WATTN_OK;
@@ -856,8 +870,41 @@ int wattn_encoder_attention(const void *x, const void *w_qkv, const float *b_qkv
                         in_dtype, batch, t, t, n_heads, 3 * d, 3 * d, d, qkv_bs, qkv_bs,
                         (int64_t)t * d, 0.125f, 0, 0, st);
   if (rc != WATTN_OK) return rc;
-  // encoder.rs:301-303: output projection
-  return launch_linear(attn, w_out, b_out, y, in_dtype, out_dtype, rows, d, d, d, d, d, st);
+  // encoder.rs:301-304: output projection (plus the residual add when the
+  // output is the f32 residual stream being updated in place)
+  return launch_linear(attn, w_out, b_out, y, in_dtype, out_dtype, rows, d, d, d, d, d, st,
+                       add_residual ? static_cast<const float *>(y) : nullptr);
+}
+
+int wattn_encoder_attention_residual(float *x, const float *ln_w, const float *ln_b,
+                                     const void *w_qkv, const float *b_qkv, const void *w_out,
+                                     const float *b_out, int dtype, int batch, int t, int n_heads,
+                                     void *workspace, size_t workspace_bytes, void *stream) {
+  clear_error();
+  if (batch < 0 || t < 0 || n_heads <= 0)
+    return set_error(WATTN_ERR_INVALID, "encoder_attention_residual: bad sizes");
+  if (batch == 0 || t == 0) return WATTN_OK;
+  if (!x || !ln_w || !ln_b) return set_error(WATTN_ERR_INVALID, "encoder_attention_residual: NULL");
+  const int d = n_heads * kHeadDim;
+  const long long rows_ll = (long long)batch * t;
+  if (rows_ll > INT32_MAX) return set_error(WATTN_ERR_INVALID, "too many rows");
+  const int rows = (int)rows_ll;
+  const size_t need = wattn_encoder_attention_workspace_bytes(batch, t, n_heads);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255))
+    return set_error(WATTN_ERR_INVALID,
+                     "encoder_attention_residual: a 256-byte aligned workspace of %zu bytes is needed",
+                     need);
+  uint8_t *xn = reinterpret_cast<uint8_t *>(workspace) + round_up((size_t)rows * 3 * d * 2, 256) +
+                round_up((size_t)rows * d * 2, 256);
+  int rc = validate_linear(xn, w_qkv, x, dtype, dtype, rows, 3 * d, d, d, d, 3 * d);
+  if (rc == WATTN_OK) rc = validate_linear(xn, w_out, x, dtype, WATTN_F32, rows, d, d, d, d, d);
+  if (rc != WATTN_OK) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  // encoder.rs:266-274: pre-LN (eps 1e-5) into the 16-bit GEMM input
+  rc = launch_layer_norm(x, ln_w, ln_b, xn, dtype, rows, d, 1e-5f, st);
+  if (rc != WATTN_OK) return rc;
+  return encoder_attention_impl(xn, w_qkv, b_qkv, w_out, b_out, x, dtype, WATTN_F32, batch, t,
+                                n_heads, workspace, workspace_bytes, stream, true);
 }
 
 int wattn_selftest_bounded_wait(int limit_us, void *stream) {

@@ -48,7 +48,8 @@ struct LinSmem {
 
 struct LinParams {
   void *y;
-  const float *bias;  // f32 [n] or nullptr
+  const float *bias;      // f32 [n] or nullptr
+  const float *residual;  // f32 [m][n] (row stride y_rs) added to y, or nullptr; may be y
   int64_t y_rs;
   int m, n, k;
   int tiles_n, n_tiles;  // tiles along n; all tiles (row-tile major)
@@ -189,6 +190,12 @@ __global__ void __launch_bounds__(kLinThreads, 1)
             v[e] = __uint_as_float(r[e]) +
                    ((p.bias != nullptr && col < p.n) ? __ldg(p.bias + col) : 0.f);
           }
+          if (p.residual != nullptr) {  // y may alias it: each element is read before it is written
+            const float *res = p.residual + (int64_t)row * p.y_rs + c0;
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (c0 + e < p.n) v[e] += res[e];
+          }
           OutT *dst = yrow + c0;
           if (c0 + 32 <= p.n && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
             if constexpr (sizeof(OutT) == 4) {
@@ -248,7 +255,7 @@ int launch_linear_typed(const CUtensorMap &mx, const CUtensorMap &mw, const LinP
 
 int launch_linear(const void *x, const void *w, const float *bias, void *y, int in_dtype,
                   int out_dtype, int m, int n, int k, int64_t x_rs, int64_t w_rs, int64_t y_rs,
-                  cudaStream_t stream) {
+                  cudaStream_t stream, const float *residual) {
   if (m == 0 || n == 0) return WATTN_OK;
   const long long tiles_m = (m + kLinBM - 1) / kLinBM, tiles_n = (n + kLinBN - 1) / kLinBN;
   if (tiles_m * tiles_n > 2147483647LL)
@@ -264,6 +271,7 @@ int launch_linear(const void *x, const void *w, const float *bias, void *y, int 
   LinParams p;
   p.y = y;
   p.bias = bias;
+  p.residual = residual;
   p.y_rs = y_rs;
   p.m = m;
   p.n = n;
@@ -282,6 +290,54 @@ int launch_linear(const void *x, const void *w, const float *bias, void *y, int 
   WATTN_LIN_CASE(WATTN_BF16, WATTN_BF16)
 #undef WATTN_LIN_CASE
   return set_error(WATTN_ERR_INVALID, "linear: 16-bit inputs only");
+}
+
+// ---------------------------------------------------------------- layer norm
+namespace {
+
+// layer_norm_row (crates/tensor/src/ops/norm.rs:67-98, the scalar order):
+// mean, population variance around it, y = (x - mean) / sqrt(var + eps) *
+// gamma + beta; one warp per row, f32 statistics, 16-bit output for the
+// projection that follows.
+template <typename OutT>
+__global__ void __launch_bounds__(256)
+    layer_norm_kernel(const float *x, const float *gamma, const float *beta, OutT *y, int rows,
+                      int d, float eps) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float *xr = x + (int64_t)row * d;
+  float sum = 0.f;
+  for (int i = lane; i < d; i += 32) sum += xr[i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float mean = sum / (float)d;
+  float sq = 0.f;
+  for (int i = lane; i < d; i += 32) {
+    const float t = xr[i] - mean;
+    sq = fmaf(t, t, sq);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  const float inv_std = 1.0f / sqrtf(sq / (float)d + eps);
+  OutT *yr = y + (int64_t)row * d;
+  for (int i = lane; i < d; i += 32)
+    yr[i] = from_f32<OutT>((xr[i] - mean) * inv_std * __ldg(gamma + i) + __ldg(beta + i));
+}
+
+}  // namespace
+
+int launch_layer_norm(const float *x, const float *gamma, const float *beta, void *y, int out_dtype,
+                      int rows, int d, float eps, cudaStream_t stream) {
+  if (rows == 0) return WATTN_OK;
+  const dim3 grid((rows + 7) / 8);
+  if (out_dtype == WATTN_F16)
+    layer_norm_kernel<__half><<<grid, 256, 0, stream>>>(x, gamma, beta, (__half *)y, rows, d, eps);
+  else if (out_dtype == WATTN_BF16)
+    layer_norm_kernel<__nv_bfloat16>
+        <<<grid, 256, 0, stream>>>(x, gamma, beta, (__nv_bfloat16 *)y, rows, d, eps);
+  else
+    return set_error(WATTN_ERR_INVALID, "layer_norm: 16-bit output only");
+  return check_launch("layer_norm");
 }
 
 }  // namespace wattn

@@ -53,9 +53,13 @@ int launch_attn_f32(const float *q, const float *k, const float *v, float *o, in
 // y[m][n] = x[m][k] W[n][k]^T (+ bias[n]) on the tensor cores (linear_tc.cu);
 // x and W 16-bit of the same type, 16-byte aligned, row strides whose byte
 // size is a multiple of 16.
+// residual (f32, row stride y_rs, may be y itself) is added when non-null.
 int launch_linear(const void *x, const void *w, const float *bias, void *y, int in_dtype,
                   int out_dtype, int m, int n, int k, int64_t x_rs, int64_t w_rs, int64_t y_rs,
-                  cudaStream_t stream);
+                  cudaStream_t stream, const float *residual = nullptr);
+// LayerNorm of f32 rows [rows][d] into 16-bit rows (linear_tc.cu).
+int launch_layer_norm(const float *x, const float *gamma, const float *beta, void *y, int out_dtype,
+                      int rows, int d, float eps, cudaStream_t stream);
 
 // Zero-fills a strided [batch][t][n_heads*64] output (t_kv == 0 case).
 int launch_zero_rows(void *o, int out_dtype, int batch, int t, int width, int64_t o_rs,

@@ -73,6 +73,8 @@ _SIGS = {
     "wattn_encoder_attention_workspace_bytes": (_sz, [_i, _i, _i]),
     "wattn_encoder_attention": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz,
                                      _vp]),
+    "wattn_encoder_attention_residual": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i,
+                                              _vp, _sz, _vp]),
     "wattn_kv_create": (_i, [ctypes.POINTER(_vp), _i, _i, _i, _i, _i, _i, _i, _i]),
     "wattn_kv_destroy": (_i, [_vp]),
     "wattn_kv_clear": (_i, [_vp]),
@@ -356,6 +358,17 @@ def encoder_attention(x, w_qkv, b_qkv, w_out, b_out, y, *, batch, t, n_heads, wo
                                        n_heads, _dev(workspace),
                                        workspace.numel() * workspace.element_size(),
                                        _stream_ptr(stream)), "encoder_attention")
+
+
+def encoder_attention_residual(x, ln_w, ln_b, w_qkv, b_qkv, w_out, b_out, *, batch, t, n_heads,
+                               workspace, stream=None) -> None:
+    """``wattn_encoder_attention_residual``: x (f32, updated in place) +=
+    the attention sub-block of an encoder layer (encoder.rs:266-304)."""
+    _check(lib.wattn_encoder_attention_residual(
+        _dev(x), _dev(ln_w), _dev(ln_b), _dev(w_qkv), _dev(b_qkv), _dev(w_out), _dev(b_out),
+        _dt_of(w_qkv), batch, t, n_heads, _dev(workspace),
+        workspace.numel() * workspace.element_size(), _stream_ptr(stream)),
+        "encoder_attention_residual")
 
 
 def decode_fwd_noalloc(q, k, v, o, *, n_groups, group_size, t_kv, n_heads, scale,
