@@ -67,6 +67,65 @@ def test_tc_whisper_shapes(W, oracle, dt, cfg):
     check_16bit(out, ref, f"{cfg}", dt)
 
 
+@pytest.mark.parametrize("cfg", [(1, 128, 4000, 1), (2, 300, 1500, 6), (3, 700, 700, 5),
+                                 (1, 256, 200, 3)],
+                         ids=lambda c: "b{}_tq{}_tkv{}_h{}".format(*c))
+def test_tc_key_split_schedule(W, oracle, cfg):
+    """Too few units for the SMs: each unit's key tiles are shared out among
+    CTAs (up to 32 parts here, ragged last tile included) and the last part
+    to finish merges the others' partials."""
+    b, t_q, t_kv, h = cfg
+    d = h * 64
+    (qd, qf), (kd, kf), (vd, vf) = (rounded(randn(s, b * t * d), 2)
+                                    for s, t in ((81, t_q), (82, t_kv), (83, t_kv)))
+    ref = oracle.flash_attention_2_batched(qf, kf, vf, b, t_q, t_kv, h, d, False)
+    for out_dt in (0, 2):
+        out = _run_fwd(W, qd, kd, vd, out_dt, b, t_q, t_kv, h)
+        check_16bit(out, ref, f"{cfg} out={out_dt}", out_dt)
+    # the same call again: the split counters were left at zero
+    out = _run_fwd(W, qd, kd, vd, 0, b, t_q, t_kv, h)
+    check_16bit(out, ref, f"{cfg} again")
+
+
+def test_tc_large_v3_shard_of_eight(W, oracle):
+    # Config 3 as one of 8 GPUs runs it: 4 utterances, 480 units on the SMs,
+    # so units are cut between CTAs. Parity on the first and the last.
+    import torch
+    b, t, h = 4, 1500, 20
+    d = h * 64
+    g = torch.Generator().manual_seed(8)
+    q, k, v = (torch.randn(b * t * d, generator=g).to(torch.bfloat16) for _ in range(3))
+    o = torch.empty(b * t * d, dtype=torch.bfloat16, device="cuda")
+    W.attention_fwd(q.cuda(), k.cuda(), v.cuda(), o, batch=b, t_q=t, t_kv=t, n_heads=h,
+                    scale=0.125)
+    torch.cuda.synchronize()
+    out = o.float().cpu().numpy().reshape(b, t * d)
+    for u in (0, 3):
+        sl = slice(u * t * d, (u + 1) * t * d)
+        ref = oracle.flash_attention_2(q[sl].float().numpy(), k[sl].float().numpy(),
+                                       v[sl].float().numpy(), t, t, h, d, False)
+        check_16bit(out[u], ref, f"utterance {u}", 2)
+
+
+def test_attention_host_two_streams(W, oracle):
+    """wattn_attention_host (the bench's end-to-end call): 6 large-v3
+    utterances in chunks of 4 and 2 on two streams, each chunk's kernel with
+    its own split partials. Parity on one utterance of each chunk."""
+    import torch
+    b, t, h = 6, 1500, 20
+    d = h * 64
+    g = torch.Generator().manual_seed(9)
+    q, k, v = (torch.randn(b * t * d, generator=g).to(torch.bfloat16) for _ in range(3))
+    o = torch.empty(b * t * d, dtype=torch.bfloat16)
+    W.attention_host(q, k, v, o, b, t, t, h, 0.125)
+    out = o.float().numpy().reshape(b, t * d)
+    for u in (1, 5):
+        sl = slice(u * t * d, (u + 1) * t * d)
+        ref = oracle.flash_attention_2(q[sl].float().numpy(), k[sl].float().numpy(),
+                                       v[sl].float().numpy(), t, t, h, d, False)
+        check_16bit(out[u], ref, f"host utterance {u}", 2)
+
+
 def test_tc_fused_qkv_buffer(W, oracle):
     # The encoder's fused QKV output [T, 3*d_model] (encoder.rs:276-286) is
     # consumed in place through row strides, without the split copy.

@@ -300,7 +300,8 @@ int validate_attention(const void *q, const void *k, const void *v, const void *
 int attention_device(const void *q, const void *k, const void *v, void *o, int in_dt, int out_dt,
                      int batch, int t_q, int t_kv, int n_heads, int64_t q_rs, int64_t kv_rs,
                      int64_t o_rs, int64_t q_bs, int64_t kv_bs, int64_t o_bs, float scale,
-                     int causal, int q_pos_offset, cudaStream_t st) {
+                     int causal, int q_pos_offset, cudaStream_t st, void *split_ws = nullptr,
+                     size_t split_ws_bytes = 0) {
   if (batch == 0 || t_q == 0) return WATTN_OK;
   if (t_kv == 0) return launch_zero_rows(o, out_dt, batch, t_q, n_heads * kHeadDim, o_rs, o_bs, st);
   if (in_dt == WATTN_F32)
@@ -308,7 +309,8 @@ int attention_device(const void *q, const void *k, const void *v, void *o, int i
                            t_q, t_kv, n_heads, q_rs, kv_rs, o_rs, q_bs, kv_bs, o_bs, scale,
                            causal, q_pos_offset, st);
   return launch_attn_tc(q, k, v, o, in_dt, out_dt, batch, t_q, t_kv, n_heads, q_rs, kv_rs, o_rs,
-                        q_bs, kv_bs, o_bs, scale, causal, q_pos_offset, st);
+                        q_bs, kv_bs, o_bs, scale, causal, q_pos_offset, st, split_ws,
+                        split_ws_bytes);
 }
 
 int validate_decode(const void *q, const void *k, const void *v, const void *o, int q_dt,
@@ -419,6 +421,17 @@ int attention_host(const void *q, const void *k, const void *v, void *o, int in_
   for (int i = 0; i < 2; ++i)
     if ((rc = grow(&h->buf[i], &h->buf_bytes[i], per * chunk, false, h->st[i])) != WATTN_OK)
       return finish_host(h, rc);
+  // Each stream's kernels keep their key-tile split partials apart.
+  if (in_dt != WATTN_F32) {
+    int dev = 0, n_sm = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return finish_host(h, check_launch("attention_host: device query"));
+    for (int i = 0; i < 2; ++i)
+      if ((rc = grow(&h->ws[i], &h->ws_bytes[i], attn_split_workspace_bytes(n_sm), true,
+                     h->st[i])) != WATTN_OK)
+        return finish_host(h, rc);
+  }
   for (int c0 = 0, ci = 0; c0 < batch; c0 += chunk, ++ci) {
     const int nb = std::min(chunk, batch - c0);
     cudaStream_t st = h->st[ci & 1];
@@ -435,7 +448,8 @@ int attention_host(const void *q, const void *k, const void *v, void *o, int in_
     }
     if (rc == WATTN_OK)
       rc = attention_device(dq, dk, dv, dout, in_dt, out_dt, nb, t_q, t_kv, n_heads, w, w, w, qbs,
-                            kvbs, obs, scale, causal, q_pos_offset, st);
+                            kvbs, obs, scale, causal, q_pos_offset, st, h->ws[ci & 1],
+                            h->ws_bytes[ci & 1]);
     for (int b = 0; b < nb && rc == WATTN_OK; ++b)
       rc = d2h((uint8_t *)o + (c0 + b) * ob, dout + round_up(ob, 256) * b, ob, st);
     if (rc != WATTN_OK) break;
@@ -819,8 +833,16 @@ size_t wattn_encoder_attention_workspace_bytes(int batch, int t, int n_heads) {
   if (batch <= 0 || t <= 0 || n_heads <= 0) return 0;
   const size_t rows = (size_t)batch * t, d = (size_t)n_heads * kHeadDim;
   // fused QKV [rows][3d], the attention output [rows][d] and (for the
-  // residual form) the normalised rows [rows][d], 16-bit each
-  return round_up(rows * 3 * d * 2, 256) + 2 * round_up(rows * d * 2, 256);
+  // residual form) the normalised rows [rows][d], 16-bit each; then the
+  // attention's key-tile split partials (sized for the current device)
+  int dev = 0, n_sm = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    cudaGetLastError();
+    n_sm = 148;
+  }
+  return round_up(rows * 3 * d * 2, 256) + 2 * round_up(rows * d * 2, 256) +
+         round_up(attn_split_workspace_bytes(n_sm), 256);
 }
 
 static int encoder_attention_impl(const void *x, const void *w_qkv, const float *b_qkv,
@@ -866,9 +888,11 @@ static int encoder_attention_impl(const void *x, const void *w_qkv, const float 
   // encoder.rs:281-299: attention reads q, k, v in place (row stride 3d),
   // without the split copy; scale 1/sqrt(64) as flash_attention_2 uses
   const int64_t qkv_bs = (int64_t)t * 3 * d;
+  uint8_t *split = attn + 2 * round_up((size_t)rows * d * 2, 256);
+  const size_t split_bytes = workspace_bytes - (size_t)(split - qkv);
   rc = attention_device(qkv, qkv + (size_t)d * 2, qkv + (size_t)2 * d * 2, attn, in_dtype,
                         in_dtype, batch, t, t, n_heads, 3 * d, 3 * d, d, qkv_bs, qkv_bs,
-                        (int64_t)t * d, 0.125f, 0, 0, st);
+                        (int64_t)t * d, 0.125f, 0, 0, st, split, split_bytes);
   if (rc != WATTN_OK) return rc;
   // encoder.rs:301-304: output projection (plus the residual add when the
   // output is the f32 residual stream being updated in place)

@@ -11,8 +11,10 @@
 //     buffers carry over from unit to unit, so the next unit's Q and first
 //     K/V tiles load and its first scores are computed while the current
 //     unit's last softmax and epilogue run;
-//   * a TMA warp streams 128-key K and V tiles through a 3-deep ring in
-//     shared memory (128-byte swizzle, the layout UMMA reads directly);
+//   * a TMA warp streams 128-key K and V tiles through a 4-deep ring in
+//     shared memory (128-byte swizzle, the layout UMMA reads directly); the
+//     query tiles are double-buffered, so the next unit's Q is resident
+//     before the current unit ends;
 //   * an MMA warp issues tcgen05.mma: S = Q K^T (M=128, N=128, K=64) into
 //     tensor memory, then O += P V (M=128, N=64, K=128) with P read back from
 //     tensor memory. S(t, j+1) is issued as soon as the softmax has taken
@@ -23,6 +25,12 @@
 //     (exp2 domain), rescales O in TMEM only when the max grows by more than
 //     2^8 (the result is exact either way: p never exceeds 256), and writes P
 //     as packed 16-bit pairs back to TMEM.
+//
+// When whole units would leave SMs idle at the end (few utterances or heads
+// per GPU), the units' key tiles are instead shared out evenly: each CTA
+// takes a run of key tiles, a unit cut by a CTA boundary is computed in
+// parts, and the part counted in last merges them (log-sum-exp); a merge
+// warp does that while the softmax warps go on.
 //
 // Tensor memory per CTA (512 columns): tile t uses S at 256t (128 columns),
 // P at 256t+128 (64 columns of packed pairs), O at 256t+192 (64 columns).
@@ -45,11 +53,13 @@ constexpr int kBN = 128;                 // keys per tile
 constexpr int kTiles = 2;                // query tiles per CTA
 constexpr int kStages = 4;               // K/V ring depth
 constexpr int kTileBytes = 128 * 128;    // 128 rows x 64 x 16-bit
-constexpr int kTmaWarp = 4 * kTiles;     // warp 8
-constexpr int kMmaWarp = kTmaWarp + 1;   // warp 9
-constexpr int kThreads = (kMmaWarp + 1) * 32;
+constexpr int kTmaWarp = 4 * kTiles;      // warp 8
+constexpr int kMmaWarp = kTmaWarp + 1;    // warp 9
+constexpr int kMergeWarp = kMmaWarp + 1;  // warp 10: counts and merges split units' parts
+constexpr int kThreads = (kMergeWarp + 1) * 32;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+constexpr int kAttnPartFloats = 66 * kBM;  // one tile's partial: O [64][128], m [128], l [128]
 // One pair of exponentials in every kFmaExp2Every is computed on the FMA
 // pipe (exp2_fma2) instead of the SFU; 0 keeps them all on the SFU (the
 // faster setting measured so far on B200).
@@ -62,10 +72,10 @@ WATTN_DEVINL constexpr bool fma_exp2_slot(int i) {
 }
 
 struct Smem {
-  uint8_t q[kTiles][kTileBytes];
+  uint8_t q[2][kTiles][kTileBytes];  // two chunks' query tiles: the next loads during this one
   uint8_t k[kStages][kTileBytes];
   uint8_t v[kStages][kTileBytes];
-  uint64_t q_full, q_empty;  // Q tiles loaded / the unit's last S done (Q may be replaced)
+  uint64_t q_full[2], q_empty[2];  // Q tiles loaded / the chunk's last S done (Q may be replaced)
   uint64_t k_full[kStages], k_empty[kStages];
   uint64_t v_full[kStages], v_empty[kStages];
   uint64_t s_full[kTiles];  // S(t, j) in TMEM (MMA commit)
@@ -73,9 +83,33 @@ struct Smem {
   uint64_t p_full[kTiles];  // P(t, j) in TMEM and O(t) rescaled (softmax arrivals)
   uint64_t o_done[kTiles];  // PV(t, j) complete: P(t, j+1) may be written (MMA commit)
   uint64_t o_free[kTiles];  // the epilogue has read O(t): the next unit may overwrite it
+  // Split chunks (at most two per CTA, its first two): the warpgroup's
+  // partial rows of chunk i are written (all its threads; completes once).
+  uint64_t part_bar[kTiles][2];
+  uint64_t merge_bar[kTiles];  // merge_flag[t] is set (once, for the CTA's last chunk)
   uint64_t drain;
   uint32_t tmem_base;
+  int merge_flag[kTiles];      // 1: this part arrived last and merges; 0: done; -1: timed out
   int abort;
+};
+
+// Division by a run-time invariant divisor d in [1, 2^31] through a
+// multiply-high (Granlund and Montgomery, "Division by invariant integers
+// using multiplication", PLDI 1994): with l = ceil(log2 d) and
+// mul = floor(2^32 (2^l - d) / d) + 1, x / d = (mulhi(x, mul) + x) >> l for
+// every dividend x < 2^31. The persistent CTAs map unit and key-tile indices
+// with it at every unit boundary.
+struct FastDiv {
+  uint32_t d, mul, shift;
+  static FastDiv make(uint32_t d) {
+    FastDiv f;
+    f.d = d;
+    f.shift = 0;
+    while ((1ull << f.shift) < d) ++f.shift;
+    f.mul = (uint32_t)((((1ull << 32) * ((1ull << f.shift) - d)) / d) + 1);
+    return f;
+  }
+  WATTN_DEVINL uint32_t div(uint32_t x) const { return (__umulhi(x, mul) + x) >> shift; }
 };
 
 // Wait sites (kernel 1): role << 16 | barrier << 8 | iteration.
@@ -86,8 +120,18 @@ struct Params {
   int64_t o_rs, o_bs;
   int t_q, t_kv;
   int n_qblk, n_heads, n_units;  // work units: (query block, head, utterance)
+  FastDiv by_qblk, by_heads;     // divisions by n_qblk and n_heads
   float scale_log2;  // scale * log2(e)
   int causal, q_pos_offset;
+  // Key-tile split schedule (0: whole units dealt round-robin). Each CTA
+  // takes the next sk_tiles key tiles of the unit-major sequence of all
+  // units' tiles (nkv_unit per unit); a unit cut by a CTA boundary is
+  // finished by the last of its parts to arrive, which merges the others'
+  // partials (part, kAttnPartFloats per slot) counted in cnt.
+  int sk_tiles, nkv_unit;
+  FastDiv by_tiles, by_nkv;  // divisions by sk_tiles and nkv_unit (the split schedule)
+  float *part;
+  int *cnt;
   int *status;
 };
 
@@ -114,22 +158,137 @@ WATTN_DEVINL void store_row(OutT *dst, const uint32_t (&o)[2][32], float inv) {
 }
 
 // Work unit u of the persistent grid: query block fastest, then head, then
-// utterance, so the units running at once share their K/V rows in L2.
+// utterance, so the units running at once share their K/V rows in L2. A
+// chunk is the part of a unit one CTA computes: key tiles [kv_lo, kv_lo+nkv)
+// of it, part `part` of n_parts (n_parts == 1: the whole unit).
 struct Unit {
-  int q0, head, b, n_tiles, nkv;
+  int q0, head, b, n_tiles, kv_lo, nkv;
+  int parts;  // n_parts | part << 16 (n_parts == 1: the whole unit)
+  int c0x;    // first CTA holding the unit << 1 | whether the unit starts inside its range
+  WATTN_DEVINL int n_parts() const { return parts & 0xffff; }
+  WATTN_DEVINL int part() const { return parts >> 16; }
+  // Partial slot of part j: the CTA c0 + j holding it keeps two slots, its
+  // first chunk's (2c) and its last chunk's (2c + 1). Part 0 is its CTA's
+  // last chunk unless the unit starts exactly at that CTA's range.
+  WATTN_DEVINL int slot(int j) const { return 2 * ((c0x >> 1) + j) + (j == 0 ? (c0x & 1) : 0); }
 };
 
 WATTN_DEVINL Unit unit_of(const Params &p, int u) {
   Unit w;
-  const int qb = u % p.n_qblk, rest = u / p.n_qblk;
-  w.head = rest % p.n_heads;
-  w.b = rest / p.n_heads;
+  const int rest = (int)p.by_qblk.div((uint32_t)u), qb = u - rest * p.n_qblk;
+  w.b = (int)p.by_heads.div((uint32_t)rest);
+  w.head = rest - w.b * p.n_heads;
   w.q0 = qb * (kBM * kTiles);
   w.n_tiles = min(kTiles, (p.t_q - w.q0 + kBM - 1) / kBM);
   int kv_end = p.t_kv;
   if (p.causal) kv_end = min(kv_end, min(w.q0 + kBM * kTiles, p.t_q) + p.q_pos_offset);
+  w.kv_lo = 0;
   w.nkv = kv_end > 0 ? (kv_end + kBN - 1) / kBN : 0;
+  w.parts = 1;
+  w.c0x = 0;
   return w;
+}
+
+// The k-th chunk of this CTA, or false past its last. Under the split
+// schedule a CTA's key range [lo, hi) covers whole units and at most two cut
+// ones, its first and its last; those two come first, so that their parts
+// are merged while the CTA works on whole units.
+WATTN_DEVINL bool chunk_at(const Params &p, int k, Unit &w) {
+  if (p.sk_tiles == 0) {
+    const long long u = (long long)blockIdx.x + (long long)k * gridDim.x;
+    if (u >= p.n_units) return false;
+    w = unit_of(p, (int)u);
+    return true;
+  }
+  // Key-tile positions are below 2^31 (the host takes the split schedule
+  // only then).
+  const uint32_t T = (uint32_t)p.sk_tiles, n = (uint32_t)p.nkv_unit;
+  const uint32_t lo = blockIdx.x * T;
+  const uint32_t hi = min(lo + T, (uint32_t)p.n_units * n);
+  if (lo >= hi) return false;
+  const uint32_t u0 = p.by_nkv.div(lo), u1 = p.by_nkv.div(hi - 1);
+  const int n_ch = (int)(u1 - u0 + 1);
+  if (k >= n_ch) return false;
+  const int cut0 = (lo != u0 * n || hi < (u0 + 1) * n) ? 1 : 0;  // first chunk is cut
+  const int cut1 = (n_ch > 1 && hi != (u1 + 1) * n) ? 1 : 0;     // last chunk is cut
+  int idx;  // position in key order
+  if (k < cut0 + cut1)
+    idx = (k == 0 && cut0) ? 0 : n_ch - 1;
+  else
+    idx = cut0 + (k - cut0 - cut1);
+  const uint32_t u = u0 + idx, ub = u * n;
+  w = unit_of(p, (int)u);
+  const uint32_t a = max(lo, ub), e = min(hi, ub + n);
+  w.kv_lo = (int)(a - ub);
+  w.nkv = (int)(e - a);
+  const uint32_t c0 = p.by_tiles.div(ub);
+  w.c0x = (int)(c0 << 1) | (ub != c0 * T ? 1 : 0);
+  w.parts = ((int)(p.by_tiles.div(ub + n - 1) - c0) + 1) | (((int)blockIdx.x - (int)c0) << 16);
+  return true;
+}
+
+// Partial of part j, query tile t: O [64][128], then m [128] and l [128].
+WATTN_DEVINL float *part_of(const Params &p, const Unit &w, int j, int t) {
+  return p.part + (size_t)(w.slot(j) * kTiles + t) * kAttnPartFloats;
+}
+
+// Counts a finished part of a split unit's tile t (one thread, after the
+// part's rows are written): true when it was the last of the unit's parts.
+WATTN_DEVINL int count_part(const Params &p, const Unit &w, int t) {
+  __threadfence();  // the part's rows, then the count (release)
+  int *cnt = p.cnt + (w.c0x >> 1) * kTiles + t;
+  const int last = atomicAdd(cnt, 1) == w.n_parts() - 1 ? 1 : 0;
+  if (last) {
+    __threadfence();     // the other parts' rows (acquire)
+    atomicExch(cnt, 0);  // every launch leaves its counters at zero
+  }
+  return last;
+}
+
+// One output row of a split unit from all its parts' partials
+// (attention.rs:228-240 over the union of the parts' keys): the offsets m of
+// the parts that saw keys are rescaled to the largest.
+template <typename OutT>
+WATTN_DEVINL void merge_row(const Params &p, const Unit &w, int t, int row, OutT *dst) {
+  constexpr int kNear = 4;  // parts whose offsets stay in registers (most units have 2 to 4)
+  const int np = w.n_parts();
+  float mj[kNear], lj[kNear];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < kNear; ++j) {
+    const float *pj = part_of(p, w, j < np ? j : 0, t);
+    mj[j] = __ldcg(pj + 64 * kBM + row);
+    lj[j] = j < np ? __ldcg(pj + 65 * kBM + row) : 0.f;
+  }
+#pragma unroll
+  for (int j = 0; j < kNear; ++j)
+    if (lj[j] > 0.f) mx = fmaxf(mx, mj[j]);
+  for (int j = kNear; j < np; ++j) {
+    const float *pj = part_of(p, w, j, t);
+    if (__ldcg(pj + 65 * kBM + row) > 0.f) mx = fmaxf(mx, __ldcg(pj + 64 * kBM + row));
+  }
+  float acc[64];
+#pragma unroll
+  for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+  float lsum = 0.f;
+  auto add_part = [&](int j, float m_j, float l_j) {
+    if (!(l_j > 0.f)) return;
+    const float aj = ex2(m_j - mx);
+    lsum += l_j * aj;
+    const float *pj = part_of(p, w, j, t);
+#pragma unroll
+    for (int i = 0; i < 64; ++i) acc[i] = fmaf(aj, __ldcg(pj + i * kBM + row), acc[i]);
+  };
+#pragma unroll
+  for (int j = 0; j < kNear; ++j) add_part(j, mj[j], lj[j]);
+  for (int j = kNear; j < np; ++j) {
+    const float *pj = part_of(p, w, j, t);
+    add_part(j, __ldcg(pj + 64 * kBM + row), __ldcg(pj + 65 * kBM + row));
+  }
+  uint32_t o[2][32];
+#pragma unroll
+  for (int i = 0; i < 64; ++i) o[i >> 5][i & 31] = __float_as_uint(acc[i]);
+  store_row<OutT>(dst, o, lsum > 0.f ? 1.f / lsum : 0.f);
 }
 
 template <int IN_DT, int OUT_DT>
@@ -145,8 +304,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    mbar_init(&s.q_full, 1);
-    mbar_init(&s.q_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.q_full[i], 1);
+      mbar_init(&s.q_empty[i], 1);
+    }
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&s.k_full[i], 1);
       mbar_init(&s.k_empty[i], 1);
@@ -159,6 +320,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s.p_full[t], kBM);
       mbar_init(&s.o_done[t], 1);
       mbar_init(&s.o_free[t], kBM);
+      mbar_init(&s.part_bar[t][0], kBM);
+      mbar_init(&s.part_bar[t][1], kBM);
+      mbar_init(&s.merge_bar[t], 1);
     }
     mbar_init(&s.drain, 1);
     s.abort = 0;
@@ -185,16 +349,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       int n_units = 0;
       int last_k = -1, last_v = -1;  // ring positions of the last tiles issued, for the wind-down
       bool ok = true;
-      for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x) {
-        const Unit w = unit_of(p, u);
+      Unit w;
+      for (int kc = 0; ok && chunk_at(p, kc, w); ++kc) {
         if (w.nkv == 0) continue;  // (every role skips such a unit alike)
-        // The Q buffer is free once the previous unit's last S has run.
-        if (n_units > 0 &&
-            !mbar_wait(&s.q_empty, (n_units - 1) & 1, abort, p.status, TC_SITE(1, 0, n_units)))
+        // Q buffer n_units % 2 is free once the last S of the chunk before
+        // the previous one has run.
+        const int qs = n_units & 1;
+        if (n_units >= 2 && !mbar_wait(&s.q_empty[qs], ((n_units >> 1) - 1) & 1, abort, p.status,
+                                       TC_SITE(1, 0, n_units)))
           break;
-        mbar_arrive_expect_tx(&s.q_full, w.n_tiles * kTileBytes);
+        mbar_arrive_expect_tx(&s.q_full[qs], w.n_tiles * kTileBytes);
         for (int t = 0; t < w.n_tiles; ++t)
-          tma_load_4d(s.q[t], &map_q, &s.q_full, 0, w.head, w.q0 + t * kBM, w.b);
+          tma_load_4d(s.q[qs][t], &map_q, &s.q_full[qs], 0, w.head, w.q0 + t * kBM, w.b);
         for (int j = 0; j < w.nkv; ++j, ++c) {
           const int st = c % kStages;
           const uint32_t ph = (c / kStages) & 1;
@@ -203,14 +369,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           mbar_arrive_expect_tx(&s.k_full[st], kTileBytes);
-          tma_load_4d(s.k[st], &map_k, &s.k_full[st], 0, w.head, j * kBN, w.b);
+          tma_load_4d(s.k[st], &map_k, &s.k_full[st], 0, w.head, (w.kv_lo + j) * kBN, w.b);
           last_k = (int)c;
           if (!mbar_wait(&s.v_empty[st], ph ^ 1, abort, p.status, TC_SITE(1, 2, j))) {
             ok = false;
             break;
           }
           mbar_arrive_expect_tx(&s.v_full[st], kTileBytes);
-          tma_load_4d(s.v[st], &map_v, &s.v_full[st], 0, w.head, j * kBN, w.b);
+          tma_load_4d(s.v[st], &map_v, &s.v_full[st], 0, w.head, (w.kv_lo + j) * kBN, w.b);
           last_v = (int)c;
         }
         ++n_units;
@@ -233,12 +399,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t ab = IN_DT == WATTN_BF16 ? 1u : 0u;
       constexpr uint32_t idesc_s = idesc_f16(ab, kBM, kBN, 0, 0);  // Q, K both K-major
       constexpr uint32_t idesc_o = idesc_f16(ab, kBM, 64, 0, 1);   // P from TMEM, V MN-major
-      const uint32_t q_addr0 = smem_u32(s.q[0]);
+      const uint32_t q_addr0 = smem_u32(s.q[0][0]);
       const uint32_t k_addr0 = smem_u32(s.k[0]);
       const uint32_t v_addr0 = smem_u32(s.v[0]);
 
+      int qs = 0;  // Q buffer of the current chunk
       auto issue_s = [&](int t, int st) {
-        const uint32_t qa = q_addr0 + t * kTileBytes, ka = k_addr0 + st * kTileBytes;
+        const uint32_t qa = q_addr0 + (qs * kTiles + t) * kTileBytes, ka = k_addr0 + st * kTileBytes;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)  // 4 x K=16 along the head dim
           umma_ss(tmem + t * 256, smem_desc_sw128(qa + kk * 32, 16, 1024),
@@ -275,10 +442,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(&s.k_empty[st]);
         return true;
       };
-      for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x) {
-        const Unit w = unit_of(p, u);
+      Unit w;
+      for (int kc = 0; ok && chunk_at(p, kc, w); ++kc) {
         if (w.nkv == 0) continue;
-        if (!mbar_wait(&s.q_full, n_units & 1, abort, p.status, TC_SITE(2, 0, n_units))) break;
+        qs = n_units & 1;
+        if (!mbar_wait(&s.q_full[qs], (n_units >> 1) & 1, abort, p.status, TC_SITE(2, 0, n_units)))
+          break;
         if (!s_step(w, c, 0)) break;
         // Per key tile j: first S(t, j+1), as soon as the softmax has taken
         // S(t, j) into registers, so the next scores are computed while the
@@ -292,7 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             }
           } else {
-            umma_commit(&s.q_empty);  // the unit's last S: Q may be replaced
+            umma_commit(&s.q_empty[qs]);  // the chunk's last S: its Q may be replaced
           }
           if (!mbar_wait(&s.v_full[st], (cj / kStages) & 1, abort, p.status, TC_SITE(2, 2, j))) {
             ok = false;
@@ -328,6 +497,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       umma_commit(&s.drain);
       mbar_wait(&s.drain, 0, &no_abort, p.status, TC_SITE(2, 6, 0));
     }
+  } else if (warp == kMergeWarp) {
+    // ---------------------------------------------------------- split merges
+    // The CTA's split chunks other than its last: each tile's part is
+    // counted in once the softmax warpgroup has written it and, when it
+    // arrived last, merged with the unit's other parts, while the softmax
+    // warps go on with the next chunk.
+    Unit w, nx;
+    bool ok = true;
+    for (int kc = 0; ok && kc < 2 && chunk_at(p, kc, w); ++kc) {
+      if (w.n_parts() == 1 || !chunk_at(p, kc + 1, nx)) break;
+      for (int t = 0; t < w.n_tiles; ++t) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&s.part_bar[t][kc], 0, abort, p.status,
+                                               TC_SITE(5, t, kc)))) {
+          ok = false;
+          break;
+        }
+        int flag = lane == 0 ? count_part(p, w, t) : 0;
+        if (!__shfl_sync(0xffffffffu, flag, 0)) continue;
+        OutT *out = reinterpret_cast<OutT *>(p.o) + (int64_t)w.b * p.o_bs + w.head * kHeadDim;
+        for (int row = lane; row < kBM; row += 32) {
+          const int qrow = w.q0 + t * kBM + row;
+          if (qrow < p.t_q) merge_row<OutT>(p, w, t, row, out + (int64_t)qrow * p.o_rs);
+        }
+      }
+    }
   } else {
     // ---------------------------------------------------------- softmax + epilogue
     const int t = warp >> 2;   // query tile of this warpgroup
@@ -339,11 +533,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float c = p.scale_log2;
     uint32_t n_s = 0, n_p = 0;  // S tiles read and P tiles written by this warpgroup
     bool ok = true;
-    for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x) {
-      const Unit w = unit_of(p, u);
+    Unit w;
+    for (int kc = 0; ok && chunk_at(p, kc, w); ++kc) {
       if (w.nkv == 0 || t >= w.n_tiles) continue;
       const int qrow = w.q0 + t * kBM + row;
-      const int key_lim = p.causal ? min(p.t_kv, qrow + p.q_pos_offset + 1) : p.t_kv;
+      // keys of this chunk visible to the row, counted from its first tile
+      const int key_lim = (p.causal ? min(p.t_kv, qrow + p.q_pos_offset + 1) : p.t_kv) -
+                          w.kv_lo * kBN;
       float m = -INFINITY, l = 0.f;
       for (int j = 0; j < w.nkv; ++j, ++n_s) {
         const bool got =
@@ -483,12 +679,51 @@ __global__ void __launch_bounds__(kThreads, 1)
       reg_fence(o[1]);
       tc_fence_before();
       mbar_arrive(&s.o_free[t]);
-      if (qrow < p.t_q) {
-        const float inv = l > 0.f ? 1.f / l : 0.f;
-        OutT *dst = reinterpret_cast<OutT *>(p.o) + (int64_t)w.b * p.o_bs +
-                    (int64_t)qrow * p.o_rs + w.head * kHeadDim;
-        store_row<OutT>(dst, o, inv);
+      const bool live = qrow < p.t_q;
+      OutT *dst = reinterpret_cast<OutT *>(p.o) + (int64_t)w.b * p.o_bs + (int64_t)qrow * p.o_rs +
+                  w.head * kHeadDim;
+      if (w.n_parts() == 1) {
+        if (live) store_row<OutT>(dst, o, l > 0.f ? 1.f / l : 0.f);
+        continue;
       }
+      // ---- one part of a split unit: its partial (O, m, l of every row,
+      // [value][row] so a warp's stores are contiguous) goes to its slot;
+      // the part that is counted in last merges all of them.
+      float *mine = part_of(p, w, w.part(), t);
+      if (live) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) mine[i * kBM + row] = __uint_as_float(o[i >> 5][i & 31]);
+        mine[64 * kBM + row] = m;
+        mine[65 * kBM + row] = l;
+      }
+      // (split chunks are a CTA's first two, so kc is 0 or 1 here)
+      mbar_arrive(&s.part_bar[t][kc]);
+      {
+        Unit nx;
+        if (chunk_at(p, kc + 1, nx)) continue;  // the merge warp counts this part in
+      }
+      // The CTA's last chunk: count it in here (nothing else is left to do).
+      // The warpgroup's first warp counts; the others wait for its verdict.
+      // Whole warps wait (a lane spinning on a barrier would hold back a lane
+      // of its warp that runs another path).
+      int flag = -1;
+      if (wq == 0) {
+        const bool got = __all_sync(
+            0xffffffffu, mbar_wait(&s.part_bar[t][kc], 0, abort, p.status, TC_SITE(3 + t, 4, kc)));
+        if (got && lane == 0) flag = count_part(p, w, t);
+        flag = __shfl_sync(0xffffffffu, flag, 0);
+        if (lane == 0) {
+          s.merge_flag[t] = flag;
+          mbar_arrive(&s.merge_bar[t]);
+        }
+      } else if (mbar_wait(&s.merge_bar[t], 0, abort, p.status, TC_SITE(3 + t, 5, kc))) {
+        flag = *reinterpret_cast<volatile int *>(&s.merge_flag[t]);
+      }
+      if (!__all_sync(0xffffffffu, flag >= 0)) {
+        ok = false;
+        break;
+      }
+      if (flag == 1 && live) merge_row<OutT>(p, w, t, row, dst);
     }
   }
 
@@ -517,8 +752,10 @@ int launch_typed(const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return check_launch("attn_fwd_tc: device query");
-  dim3 grid(std::min(p.n_units, n_sm));
-  kern<<<grid, kThreads, smem, stream>>>(mq, mk, mv, p);
+  int n_ctas = std::min(p.n_units, n_sm);
+  if (p.sk_tiles > 0)
+    n_ctas = (int)(((long long)p.n_units * p.nkv_unit + p.sk_tiles - 1) / p.sk_tiles);
+  kern<<<dim3(n_ctas), kThreads, smem, stream>>>(mq, mk, mv, p);
   return check_launch("attn_fwd_tc");
 }
 
@@ -535,10 +772,37 @@ int make_qkv_map(CUtensorMap *map, const void *base, int dt, int n_heads, int t,
 
 }  // namespace
 
+// Cost model in key-tile times, fitted to B200 timings of both schedules:
+// every chunk (a unit, or a part of one) costs about 1.2 tiles more than its
+// key tiles (Q, the first scores, the epilogue). Parts are merged by one
+// warp, about five tiles after the part arrives, unseen while the CTA has
+// whole units left to compute: with fewer than 2.5 units of key tiles per
+// CTA the merges (or the softmax warps' own merge of the CTA's last chunk)
+// add about four tiles to the end. The split schedule is taken when it is
+// predicted to save 7 %.
+int plan_attn_split(long long n_units, int nkv, int n_sm, int causal) {
+  if (causal || n_units <= 0 || nkv <= 0 || n_sm <= 0) return 0;
+  const long long tiles = n_units * nkv;
+  if (tiles > INT_MAX || n_units % n_sm == 0) return 0;
+  const double c = 1.2;
+  const long long waves = (n_units + n_sm - 1) / n_sm;
+  const double whole = (double)waves * (nkv + c);
+  const long long T = (tiles + n_sm - 1) / n_sm;
+  const long long chunks = (T + nkv - 1) / nkv + 1;  // at most, per CTA
+  const double tail = T < 2.5 * nkv ? 4.0 : 1.0;
+  const double split = (double)T + (double)chunks * c + tail;
+  return split < 0.93 * whole ? (int)T : 0;
+}
+
+size_t attn_split_workspace_bytes(int n_sm) {
+  return kCounterBytes + (size_t)2 * n_sm * kTiles * kAttnPartFloats * sizeof(float);
+}
+
 int launch_attn_tc(const void *q, const void *k, const void *v, void *o, int in_dtype,
                    int out_dtype, int batch, int t_q, int t_kv, int n_heads, int64_t q_rs,
                    int64_t kv_rs, int64_t o_rs, int64_t q_bs, int64_t kv_bs, int64_t o_bs,
-                   float scale, int causal, int q_pos_offset, cudaStream_t stream) {
+                   float scale, int causal, int q_pos_offset, cudaStream_t stream,
+                   void *split_ws, size_t split_ws_bytes) {
   CUtensorMap mq, mk, mv;
   int rc;
   if ((rc = make_qkv_map(&mq, q, in_dtype, n_heads, t_q, batch, q_rs, q_bs)) != WATTN_OK) return rc;
@@ -555,12 +819,46 @@ int launch_attn_tc(const void *q, const void *k, const void *v, void *o, int in_
   p.q_pos_offset = q_pos_offset;
   p.n_qblk = (t_q + kBM * kTiles - 1) / (kBM * kTiles);
   p.n_heads = n_heads;
+  p.by_qblk = FastDiv::make((uint32_t)p.n_qblk);
+  p.by_heads = FastDiv::make((uint32_t)n_heads);
   const long long n_units = (long long)p.n_qblk * n_heads * batch;
   if (n_units > INT_MAX)
     return set_error(WATTN_ERR_INVALID, "attention: %lld work units exceed 2^31", n_units);
   p.n_units = (int)n_units;
   p.status = device_status_ptr();
   if (p.status == nullptr) return WATTN_ERR_CUDA;
+  // Key-tile split schedule when whole units would leave SMs idle at the end
+  // (few utterances or heads per GPU).
+  p.sk_tiles = 0;
+  p.nkv_unit = (t_kv + kBN - 1) / kBN;
+  p.by_tiles = FastDiv::make(1);
+  p.by_nkv = FastDiv::make((uint32_t)p.nkv_unit);
+  p.part = nullptr;
+  p.cnt = nullptr;
+  int dev = 0, n_sm = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return check_launch("attn_fwd_tc: device query");
+  const int T = plan_attn_split(n_units, p.nkv_unit, n_sm, causal);
+  if (T > 0) {
+    const long long n_ctas = ((long long)n_units * p.nkv_unit + T - 1) / T;
+    const size_t need = attn_split_workspace_bytes((int)n_ctas);
+    void *ws = split_ws;
+    if (ws != nullptr && split_ws_bytes < need) ws = nullptr;  // too small: whole units
+    if (ws != nullptr) {
+      // a caller's buffer: the counters this launch uses start at zero
+      if (cudaMemsetAsync(ws, 0, (size_t)n_ctas * kTiles * sizeof(int), stream) != cudaSuccess)
+        return check_launch("attn_fwd_tc: counter reset");
+    } else if (split_ws == nullptr) {
+      ws = thread_workspace(need, stream);
+    }
+    if (ws != nullptr) {
+      p.sk_tiles = T;
+      p.by_tiles = FastDiv::make((uint32_t)T);
+      p.cnt = reinterpret_cast<int *>(ws);
+      p.part = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(ws) + kCounterBytes);
+    }
+  }
   if (in_dtype == WATTN_F16) {
     if (out_dtype == WATTN_F32)
       return launch_typed<WATTN_F16, WATTN_F32>(mq, mk, mv, p, batch, n_heads, stream);

@@ -53,11 +53,6 @@ constexpr int kStrSlots = 148 * 3; // resident tensor-core CTAs on a B200: three
 constexpr int kStrSplitTarget = 160;
 constexpr int kStrMinSubs = 4;     // sub-tiles per split below which no further split is made
 constexpr bool kStrPagedPersist = true;  // paged entries come sorted by length
-// Workspace layout, the same for every call: [counters][partials]. The
-// counter region has a fixed size, so partials written by one call can never
-// land where a later call of another shape keeps its counters; every call
-// leaves the counters it used at zero.
-constexpr size_t kCounterBytes = (size_t)kMaxSplitCounters * sizeof(int);
 static_assert(kDecSub == kDecSubRows, "paged sub-tiles and TMA boxes must agree");
 // Paged kernels take two tensor maps, DecParams (< 128 bytes) and the table
 // by value; CUDA 12.1+ allows 32764 bytes of kernel parameters.

@@ -38,11 +38,28 @@ int check_launch(const char *what);
 // ----------------------------------------------------------- kernel launchers
 // All pointers device, strides in elements; arguments already validated.
 
-// tcgen05 tensor-core attention, 16-bit inputs (attn_tc.cu).
+// Split workspaces (decode and attention) share one layout:
+// [counters, kCounterBytes][partials]. The counter region has a fixed size,
+// so partials written by one call never land where a later call of another
+// shape keeps its counters; every launch leaves the counters it used at zero.
+constexpr int kMaxSplitCounters = 65536;
+constexpr size_t kCounterBytes = (size_t)kMaxSplitCounters * sizeof(int);
+
+// tcgen05 tensor-core attention, 16-bit inputs (attn_tc.cu). When the
+// key-tile split schedule is chosen, its partials go to split_ws (a caller's
+// buffer of split_ws_bytes whose counters this call zeroes first) or, with
+// split_ws NULL, to the calling thread's workspace; without room for them
+// whole units are dealt round-robin.
 int launch_attn_tc(const void *q, const void *k, const void *v, void *o, int in_dtype,
                    int out_dtype, int batch, int t_q, int t_kv, int n_heads, int64_t q_rs,
                    int64_t kv_rs, int64_t o_rs, int64_t q_bs, int64_t kv_bs, int64_t o_bs,
-                   float scale, int causal, int q_pos_offset, cudaStream_t stream);
+                   float scale, int causal, int q_pos_offset, cudaStream_t stream,
+                   void *split_ws = nullptr, size_t split_ws_bytes = 0);
+// Key tiles per CTA of the split schedule for n_units units of nkv key tiles
+// each on n_sm CTAs, or 0 when whole units dealt round-robin finish sooner.
+int plan_attn_split(long long n_units, int nkv, int n_sm, int causal);
+// Workspace of the split schedule on a device of n_sm SMs (its upper bound).
+size_t attn_split_workspace_bytes(int n_sm);
 
 // f32 CUDA-core attention (attn_f32.cu).
 int launch_attn_f32(const float *q, const float *k, const float *v, float *o, int batch,
@@ -66,8 +83,7 @@ int launch_zero_rows(void *o, int out_dtype, int batch, int t, int width, int64_
                      int64_t o_bs, cudaStream_t stream);
 
 // Split-KV decode over dense K/V (decode.cu). Counters of one launch are
-// indexed (row group, head) and must fit this fixed region.
-constexpr int kMaxSplitCounters = 65536;
+// indexed (row group, head) and must fit the fixed counter region.
 struct DecodePlan {
   int chunk;      // keys per split (multiple of 64)
   int n_splits;   // splits per (row chunk, head)
