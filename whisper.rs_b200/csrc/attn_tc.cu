@@ -250,7 +250,7 @@ WATTN_DEVINL int count_part(const Params &p, const Unit &w, int t) {
 // the parts that saw keys are rescaled to the largest.
 template <typename OutT>
 WATTN_DEVINL void merge_row(const Params &p, const Unit &w, int t, int row, OutT *dst) {
-  constexpr int kNear = 4;  // parts whose offsets stay in registers (most units have 2 to 4)
+  constexpr int kNear = 4;  // parts whose weights stay in registers (most units have 2 to 4)
   const int np = w.n_parts();
   float mj[kNear], lj[kNear];
   float mx = -INFINITY;
@@ -267,28 +267,61 @@ WATTN_DEVINL void merge_row(const Params &p, const Unit &w, int t, int row, OutT
     const float *pj = part_of(p, w, j, t);
     if (__ldcg(pj + 65 * kBM + row) > 0.f) mx = fmaxf(mx, __ldcg(pj + 64 * kBM + row));
   }
-  float acc[64];
-#pragma unroll
-  for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+  // part weights 2^(m_j - mx) and the merged normaliser
+  float aj[kNear];
   float lsum = 0.f;
-  auto add_part = [&](int j, float m_j, float l_j) {
-    if (!(l_j > 0.f)) return;
-    const float aj = ex2(m_j - mx);
-    lsum += l_j * aj;
-    const float *pj = part_of(p, w, j, t);
 #pragma unroll
-    for (int i = 0; i < 64; ++i) acc[i] = fmaf(aj, __ldcg(pj + i * kBM + row), acc[i]);
-  };
-#pragma unroll
-  for (int j = 0; j < kNear; ++j) add_part(j, mj[j], lj[j]);
+  for (int j = 0; j < kNear; ++j) {
+    aj[j] = lj[j] > 0.f ? ex2(mj[j] - mx) : 0.f;
+    lsum += lj[j] * aj[j];
+  }
   for (int j = kNear; j < np; ++j) {
     const float *pj = part_of(p, w, j, t);
-    add_part(j, __ldcg(pj + 64 * kBM + row), __ldcg(pj + 65 * kBM + row));
+    const float l_j = __ldcg(pj + 65 * kBM + row);
+    if (l_j > 0.f) lsum += l_j * ex2(__ldcg(pj + 64 * kBM + row) - mx);
   }
-  uint32_t o[2][32];
+  const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+  // 32 dims at a time (the merge warp runs with few registers)
+#pragma unroll 1
+  for (int h = 0; h < 2; ++h) {
+    float acc[32];
 #pragma unroll
-  for (int i = 0; i < 64; ++i) o[i >> 5][i & 31] = __float_as_uint(acc[i]);
-  store_row<OutT>(dst, o, lsum > 0.f ? 1.f / lsum : 0.f);
+    for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < kNear; ++j) {
+      if (!(aj[j] > 0.f)) continue;
+      const float *pj = part_of(p, w, j, t) + h * 32 * kBM;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) acc[i] = fmaf(aj[j], __ldcg(pj + i * kBM + row), acc[i]);
+    }
+    for (int j = kNear; j < np; ++j) {
+      const float *pj = part_of(p, w, j, t);
+      const float l_j = __ldcg(pj + 65 * kBM + row);
+      if (!(l_j > 0.f)) continue;
+      const float a = ex2(__ldcg(pj + 64 * kBM + row) - mx);
+      pj += h * 32 * kBM;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) acc[i] = fmaf(a, __ldcg(pj + i * kBM + row), acc[i]);
+    }
+    if constexpr (sizeof(OutT) == 4) {
+      float4 *d4 = reinterpret_cast<float4 *>(dst + h * 32);
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        d4[c] = make_float4(acc[4 * c] * inv, acc[4 * c + 1] * inv, acc[4 * c + 2] * inv,
+                            acc[4 * c + 3] * inv);
+    } else {
+      uint4 *d4 = reinterpret_cast<uint4 *>(dst + h * 32);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint4 v;
+        v.x = pack2<OutT>(acc[8 * c + 0] * inv, acc[8 * c + 1] * inv);
+        v.y = pack2<OutT>(acc[8 * c + 2] * inv, acc[8 * c + 3] * inv);
+        v.z = pack2<OutT>(acc[8 * c + 4] * inv, acc[8 * c + 5] * inv);
+        v.w = pack2<OutT>(acc[8 * c + 6] * inv, acc[8 * c + 7] * inv);
+        d4[c] = v;
+      }
+    }
+  }
 }
 
 template <int IN_DT, int OUT_DT>
