@@ -226,6 +226,22 @@ int d2h(void *dst, const void *src, size_t n, cudaStream_t st) {
 // Ends a host-buffer call: waits for both streams, then reports CUDA errors
 // and the device status word.
 int consume_status();
+
+// After a bounded wait ran out, a kernel may have left split counters
+// counted up: zero the counter regions of the calling thread's workspaces on
+// the current device, so that the next launch's last-part detection starts
+// clean. (Caller-owned workspaces are zeroed by the launches that use them.)
+void reset_split_counters() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return;
+  cudaDeviceSynchronize();
+  if (t_ws[dev].ptr) cudaMemset(t_ws[dev].ptr, 0, std::min(t_ws[dev].bytes, kCounterBytes));
+  HostCtx &h = t_host[dev];
+  for (int i = 0; i < 2; ++i)
+    if (h.ws[i]) cudaMemset(h.ws[i], 0, std::min(h.ws_bytes[i], kCounterBytes));
+  cudaDeviceSynchronize();
+}
+
 int finish_host(HostCtx *h, int rc) {
   for (int i = 0; i < 2; ++i)
     if (cudaStreamSynchronize(h->st[i]) != cudaSuccess && rc == WATTN_OK)
@@ -243,6 +259,7 @@ int consume_status() {
       s[0] != WATTN_OK) {
     const int zero[2] = {WATTN_OK, 0};
     cudaMemcpy(sp, zero, sizeof(zero), cudaMemcpyHostToDevice);
+    reset_split_counters();
     return set_error(s[0], "a kernel's bounded wait ran out (site 0x%08x)", s[1]);
   }
   return WATTN_OK;
@@ -561,6 +578,7 @@ int wattn_device_status(int device, int *status) {
   const int zero[2] = {WATTN_OK, 0};
   if (rc == WATTN_OK && cudaMemcpy(sp, zero, sizeof(zero), cudaMemcpyHostToDevice) != cudaSuccess)
     rc = check_launch("clear status word");
+  if (rc == WATTN_OK && s[0] != WATTN_OK) reset_split_counters();
   if (device >= 0 && device != prev) cudaSetDevice(prev);
   *status = s[0];
   if (rc == WATTN_OK && s[0] != WATTN_OK)
