@@ -369,6 +369,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // The set-up above overlaps the end of the previous kernel in the stream
+  // (launched with programmatic serialisation); global memory is read and
+  // written only after it has completed. The next launch may start its own
+  // set-up as this grid's CTAs retire.
+  grid_dep_wait();
+  grid_dep_launch();
   const uint32_t tmem = s.tmem_base;
   volatile int *abort = &s.abort;
 
@@ -788,7 +794,8 @@ int launch_typed(const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap
   int n_ctas = std::min(p.n_units, n_sm);
   if (p.sk_tiles > 0)
     n_ctas = (int)(((long long)p.n_units * p.nkv_unit + p.sk_tiles - 1) / p.sk_tiles);
-  kern<<<dim3(n_ctas), kThreads, smem, stream>>>(mq, mk, mv, p);
+  if (launch_pdl(kern, dim3(n_ctas), dim3(kThreads), smem, stream, mq, mk, mv, p) != cudaSuccess)
+    return check_launch("attn_fwd_tc (launch)");
   return check_launch("attn_fwd_tc");
 }
 

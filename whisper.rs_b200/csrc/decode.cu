@@ -805,6 +805,8 @@ template <int Q_DT, int KV_DT, int OUT_DT>
 __global__ void __launch_bounds__(kDecThreads)
     decode_dense_kernel(const __grid_constant__ CUtensorMap map_k,
                         const __grid_constant__ CUtensorMap map_v, const DecParams p) {
+  grid_dep_wait();  // (launched with programmatic serialisation)
+  grid_dep_launch();
   decode_simt_body<Q_DT, KV_DT, OUT_DT, false>(map_k, map_v, p, nullptr);
 }
 
@@ -813,6 +815,8 @@ __global__ void __launch_bounds__(kDecThreads)
     decode_paged_kernel(const __grid_constant__ CUtensorMap map_k,
                         const __grid_constant__ CUtensorMap map_v, const DecParams p,
                         const __grid_constant__ PagedTable pt) {
+  grid_dep_wait();  // (launched with programmatic serialisation)
+  grid_dep_launch();
   decode_simt_body<Q_DT, KV_DT, OUT_DT, true>(map_k, map_v, p, &pt);
 }
 
@@ -820,6 +824,8 @@ template <int DT, int OUT_DT>
 __global__ void __launch_bounds__(kStrThreads, 3)  // three CTAs per SM (shared memory allows three)
     decode_stream_dense_kernel(const __grid_constant__ CUtensorMap map_k,
                                const __grid_constant__ CUtensorMap map_v, const DecParams p) {
+  grid_dep_wait();  // (launched with programmatic serialisation)
+  grid_dep_launch();
   decode_stream_body<DT, OUT_DT, false>(map_k, map_v, p, nullptr);
 }
 
@@ -828,6 +834,8 @@ __global__ void __launch_bounds__(kStrThreads, 3)  // three CTAs per SM (shared 
     decode_stream_paged_kernel(const __grid_constant__ CUtensorMap map_k,
                                const __grid_constant__ CUtensorMap map_v, const DecParams p,
                                const __grid_constant__ PagedTable pt) {
+  grid_dep_wait();  // (launched with programmatic serialisation)
+  grid_dep_launch();
   decode_stream_body<DT, OUT_DT, true>(map_k, map_v, p, &pt);
 }
 
@@ -849,12 +857,14 @@ int launch_typed(const CUtensorMap &mk, const CUtensorMap &mv, const DecParams &
       auto kern = decode_stream_paged_kernel<KV_DT, OUT_DT>;
       int rc = set_smem(kern, smem);
       if (rc != WATTN_OK) return rc;
-      kern<<<grid, kStrThreads, smem, stream>>>(mk, mv, p, *pt);
+      if (launch_pdl(kern, grid, dim3(kStrThreads), smem, stream, mk, mv, p, *pt) != cudaSuccess)
+        return check_launch("decode_stream_paged (launch)");
     } else {
       auto kern = decode_stream_dense_kernel<KV_DT, OUT_DT>;
       int rc = set_smem(kern, smem);
       if (rc != WATTN_OK) return rc;
-      kern<<<grid, kStrThreads, smem, stream>>>(mk, mv, p);
+      if (launch_pdl(kern, grid, dim3(kStrThreads), smem, stream, mk, mv, p) != cudaSuccess)
+        return check_launch("decode_stream_dense (launch)");
     }
   } else {
     constexpr int smem = (int)sizeof(DecSmem<KV_DT>) + 1024;
@@ -862,12 +872,14 @@ int launch_typed(const CUtensorMap &mk, const CUtensorMap &mv, const DecParams &
       auto kern = decode_paged_kernel<Q_DT, KV_DT, OUT_DT>;
       int rc = set_smem(kern, smem);
       if (rc != WATTN_OK) return rc;
-      kern<<<grid, kDecThreads, smem, stream>>>(mk, mv, p, *pt);
+      if (launch_pdl(kern, grid, dim3(kDecThreads), smem, stream, mk, mv, p, *pt) != cudaSuccess)
+        return check_launch("decode_paged (launch)");
     } else {
       auto kern = decode_dense_kernel<Q_DT, KV_DT, OUT_DT>;
       int rc = set_smem(kern, smem);
       if (rc != WATTN_OK) return rc;
-      kern<<<grid, kDecThreads, smem, stream>>>(mk, mv, p);
+      if (launch_pdl(kern, grid, dim3(kDecThreads), smem, stream, mk, mv, p) != cudaSuccess)
+        return check_launch("decode_dense (launch)");
     }
   }
   return check_launch(PAGED ? "decode_paged" : "decode_dense");

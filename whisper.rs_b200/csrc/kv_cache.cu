@@ -78,6 +78,8 @@ WATTN_DEVINL void store8(T *dst, const float (&f)[8]) {
 template <typename SrcT, typename DstT, bool VEC>
 __global__ void kv_append_kernel(const SrcT *k_rows, const SrcT *v_rows, DstT *pool,
                                  const __grid_constant__ AppendTable t) {
+  grid_dep_wait();  // (launched with programmatic serialisation)
+  grid_dep_launch();
   const int r = blockIdx.x;
   const int width = t.n_heads * 64;
   const int64_t page_elems = (int64_t)t.n_layers * 2 * t.n_heads * t.page_rows * 64;
@@ -132,12 +134,12 @@ void launch_append_vec(int dst_dt, const SrcT *ks, const SrcT *vs, void *pool,
   const dim3 grid(t.n_rows);
   const int threads = VEC ? 160 : 256;  // VEC: 160 x 8 = the 1280 elements of a large-v3 row
   if (dst_dt == WATTN_F32)
-    kv_append_kernel<SrcT, float, VEC><<<grid, threads, 0, st>>>(ks, vs, (float *)pool, t);
+    launch_pdl(kv_append_kernel<SrcT, float, VEC>, grid, dim3(threads), 0, st, ks, vs, (float *)pool, t);
   else if (dst_dt == WATTN_F16)
-    kv_append_kernel<SrcT, __half, VEC><<<grid, threads, 0, st>>>(ks, vs, (__half *)pool, t);
+    launch_pdl(kv_append_kernel<SrcT, __half, VEC>, grid, dim3(threads), 0, st, ks, vs, (__half *)pool, t);
   else
-    kv_append_kernel<SrcT, __nv_bfloat16, VEC>
-        <<<grid, threads, 0, st>>>(ks, vs, (__nv_bfloat16 *)pool, t);
+    launch_pdl(kv_append_kernel<SrcT, __nv_bfloat16, VEC>, grid, dim3(threads), 0, st, ks, vs,
+               (__nv_bfloat16 *)pool, t);
 }
 
 template <typename SrcT>

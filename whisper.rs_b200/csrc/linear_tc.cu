@@ -90,6 +90,10 @@ __global__ void __launch_bounds__(kLinThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // (launched with programmatic serialisation: the set-up above overlaps the
+  // previous kernel's end; global memory only after it has completed)
+  grid_dep_wait();
+  grid_dep_launch();
   const uint32_t tmem = s.tmem_base;
   volatile int *abort = &s.abort;
 
@@ -247,7 +251,9 @@ int launch_linear_typed(const CUtensorMap &mx, const CUtensorMap &mw, const LinP
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return check_launch("linear_tc: device query");
-  kern<<<std::min(p.n_tiles, n_sm), kLinThreads, smem, stream>>>(mx, mw, p);
+  if (launch_pdl(kern, dim3(std::min(p.n_tiles, n_sm)), dim3(kLinThreads), smem, stream, mx, mw,
+                 p) != cudaSuccess)
+    return check_launch("linear_tc (launch)");
   return check_launch("linear_tc");
 }
 
@@ -303,6 +309,8 @@ template <typename OutT>
 __global__ void __launch_bounds__(256)
     layer_norm_kernel(const float *x, const float *gamma, const float *beta, OutT *y, int rows,
                       int d, float eps) {
+  grid_dep_wait();  // (launched with programmatic serialisation)
+  grid_dep_launch();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= rows) return;
   const float *xr = x + (int64_t)row * d;
@@ -331,10 +339,11 @@ int launch_layer_norm(const float *x, const float *gamma, const float *beta, voi
   if (rows == 0) return WATTN_OK;
   const dim3 grid((rows + 7) / 8);
   if (out_dtype == WATTN_F16)
-    layer_norm_kernel<__half><<<grid, 256, 0, stream>>>(x, gamma, beta, (__half *)y, rows, d, eps);
+    launch_pdl(layer_norm_kernel<__half>, grid, dim3(256), 0, stream, x, gamma, beta, (__half *)y,
+               rows, d, eps);
   else if (out_dtype == WATTN_BF16)
-    layer_norm_kernel<__nv_bfloat16>
-        <<<grid, 256, 0, stream>>>(x, gamma, beta, (__nv_bfloat16 *)y, rows, d, eps);
+    launch_pdl(layer_norm_kernel<__nv_bfloat16>, grid, dim3(256), 0, stream, x, gamma, beta,
+               (__nv_bfloat16 *)y, rows, d, eps);
   else
     return set_error(WATTN_ERR_INVALID, "layer_norm: 16-bit output only");
   return check_launch("layer_norm");

@@ -122,6 +122,15 @@ WATTN_DEVINL float2 exp2_fma2(float2 x) {
                      __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
 }
 
+// ------------------------------------------------------------ dependent launch
+// Programmatic dependent launch. grid_dep_wait: waits until the grids this
+// launch depends on have completed and their memory is visible (a no-op when
+// the launch did not ask for programmatic serialisation). grid_dep_launch:
+// lets the next such launch in the stream start its CTAs (they then run up
+// to their own grid_dep_wait) once every CTA of this grid has called it.
+WATTN_DEVINL void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+WATTN_DEVINL void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ------------------------------------------------------------ shared memory
 WATTN_DEVINL uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -6,9 +6,32 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/wattn.h"
 
 namespace wattn {
+
+// Launches a kernel with programmatic stream serialisation: its CTAs may be
+// scheduled while the previous kernel in the stream finishes, and they wait
+// for it in grid_dep_wait() before touching global memory (every kernel
+// launched this way calls it first). Copies and memsets in the stream keep
+// their full ordering.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // Records `msg` (printf-style) as the calling thread's last error and
 // returns `status`.
