@@ -56,7 +56,8 @@ constexpr int kTileBytes = 128 * 128;    // 128 rows x 64 x 16-bit
 constexpr int kTmaWarp = 4 * kTiles;      // warp 8
 constexpr int kMmaWarp = kTmaWarp + 1;    // warp 9
 constexpr int kMergeWarp = kMmaWarp + 1;  // warp 10: counts and merges split units' parts
-constexpr int kThreads = (kMergeWarp + 1) * 32;
+constexpr int kMma1Warp = kMergeWarp + 1;  // warp 11: issues tile 1's products (warp 9: tile 0's)
+constexpr int kThreads = (kMma1Warp + 1) * 32;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 constexpr int kAttnPartFloats = 66 * kBM;  // one tile's partial: O [64][128], m [128], l [128]
@@ -75,14 +76,22 @@ struct Smem {
   uint8_t q[2][kTiles][kTileBytes];  // two chunks' query tiles: the next loads during this one
   uint8_t k[kStages][kTileBytes];
   uint8_t v[kStages][kTileBytes];
-  uint64_t q_full[2], q_empty[2];  // Q tiles loaded / the chunk's last S done (Q may be replaced)
-  uint64_t k_full[kStages], k_empty[kStages];
-  uint64_t v_full[kStages], v_empty[kStages];
+  // Every unit runs both query tiles (rows past t_q are computed on the zero
+  // rows TMA fills in and not stored), so both tiles pass the same sequence
+  // of key tiles and share the K/V ring; each tile's products are issued by
+  // its own MMA warp against its own barriers.
+  // q_empty[i]: Q buffer i may be refilled — the chunk's last S of both
+  // tiles is done and both epilogues are done with the buffer (a unit's
+  // output tiles are staged there for the TMA store).
+  uint64_t q_full[2], q_empty[2];
+  uint64_t kv_full[kStages];   // the stage's K and V tiles loaded (TMA)
+  uint64_t kv_empty[kStages];  // both warpgroups saw the stage's PV complete (one arrival each)
   uint64_t s_full[kTiles];  // S(t, j) in TMEM (MMA commit)
   uint64_t s_free[kTiles];  // S(t, j) read into registers: S(t, j+1) may overwrite it
   uint64_t p_full[kTiles];  // P(t, j) in TMEM and O(t) rescaled (softmax arrivals)
   uint64_t o_done[kTiles];  // PV(t, j) complete: P(t, j+1) may be written (MMA commit)
   uint64_t o_free[kTiles];  // the epilogue has read O(t): the next unit may overwrite it
+  uint64_t ep_full[kTiles];  // every row of output tile t is staged for the TMA store
   // Split chunks (at most two per CTA, its first two): the warpgroup's
   // partial rows of chunk i are written (all its threads; completes once).
   uint64_t part_bar[kTiles][2];
@@ -133,6 +142,7 @@ struct Params {
   float *part;
   int *cnt;
   int *status;
+  int tma_out;  // whole units' output tiles leave through map_o (16-bit output)
 };
 
 // Normalises 64 accumulated dims by inv and stores them (16-byte stores).
@@ -179,7 +189,7 @@ WATTN_DEVINL Unit unit_of(const Params &p, int u) {
   w.b = (int)p.by_heads.div((uint32_t)rest);
   w.head = rest - w.b * p.n_heads;
   w.q0 = qb * (kBM * kTiles);
-  w.n_tiles = min(kTiles, (p.t_q - w.q0 + kBM - 1) / kBM);
+  w.n_tiles = kTiles;  // always both tiles (the barriers are shared by them)
   int kv_end = p.t_kv;
   if (p.causal) kv_end = min(kv_end, min(w.q0 + kBM * kTiles, p.t_q) + p.q_pos_offset);
   w.kv_lo = 0;
@@ -328,7 +338,8 @@ template <int IN_DT, int OUT_DT>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                        const __grid_constant__ CUtensorMap map_k,
-                       const __grid_constant__ CUtensorMap map_v, const Params p) {
+                       const __grid_constant__ CUtensorMap map_v,
+                       const __grid_constant__ CUtensorMap map_o, const Params p) {
   using InT = typename Elem<IN_DT>::T;
   using OutT = typename Elem<OUT_DT>::T;
   extern __shared__ uint8_t smem_raw[];
@@ -339,13 +350,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.q_full[i], 1);
-      mbar_init(&s.q_empty[i], 1);
+      // a commit from each tile's MMA warp and an arrival from each epilogue
+      mbar_init(&s.q_empty[i], 2 * kTiles);
     }
     for (int i = 0; i < kStages; ++i) {
-      mbar_init(&s.k_full[i], 1);
-      mbar_init(&s.k_empty[i], 1);
-      mbar_init(&s.v_full[i], 1);
-      mbar_init(&s.v_empty[i], 1);
+      mbar_init(&s.kv_full[i], 1);
+      mbar_init(&s.kv_empty[i], kTiles);
     }
     for (int t = 0; t < kTiles; ++t) {
       mbar_init(&s.s_full[t], 1);
@@ -353,11 +363,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s.p_full[t], kBM);
       mbar_init(&s.o_done[t], 1);
       mbar_init(&s.o_free[t], kBM);
+      mbar_init(&s.ep_full[t], kBM);
       mbar_init(&s.part_bar[t][0], kBM);
       mbar_init(&s.part_bar[t][1], kBM);
       mbar_init(&s.merge_bar[t], 1);
     }
-    mbar_init(&s.drain, 1);
+    mbar_init(&s.drain, kTiles);  // one commit from each MMA warp
     s.abort = 0;
     fence_barrier_init();
   }
@@ -386,7 +397,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&map_v);
       uint32_t c = 0;  // K/V ring position over all units of this CTA
       int n_units = 0;
-      int last_k = -1, last_v = -1;  // ring positions of the last tiles issued, for the wind-down
+      int last_kv = -1;  // ring position of the last stage loaded, for the wind-down
       bool ok = true;
       Unit w;
       for (int kc = 0; ok && chunk_at(p, kc, w); ++kc) {
@@ -403,20 +414,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < w.nkv; ++j, ++c) {
           const int st = c % kStages;
           const uint32_t ph = (c / kStages) & 1;
-          if (!mbar_wait(&s.k_empty[st], ph ^ 1, abort, p.status, TC_SITE(1, 1, j))) {
+          if (!mbar_wait(&s.kv_empty[st], ph ^ 1, abort, p.status, TC_SITE(1, 1, j))) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&s.k_full[st], kTileBytes);
-          tma_load_4d(s.k[st], &map_k, &s.k_full[st], 0, w.head, (w.kv_lo + j) * kBN, w.b);
-          last_k = (int)c;
-          if (!mbar_wait(&s.v_empty[st], ph ^ 1, abort, p.status, TC_SITE(1, 2, j))) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(&s.v_full[st], kTileBytes);
-          tma_load_4d(s.v[st], &map_v, &s.v_full[st], 0, w.head, (w.kv_lo + j) * kBN, w.b);
-          last_v = (int)c;
+          mbar_arrive_expect_tx(&s.kv_full[st], 2 * kTileBytes);
+          tma_load_4d(s.k[st], &map_k, &s.kv_full[st], 0, w.head, (w.kv_lo + j) * kBN, w.b);
+          tma_load_4d(s.v[st], &map_v, &s.kv_full[st], 0, w.head, (w.kv_lo + j) * kBN, w.b);
+          last_kv = (int)c;
         }
         ++n_units;
       }
@@ -424,117 +429,109 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Wind-down after a timeout: let the loads still in flight land
         // before the CTA's shared memory is released (bounded waits).
         volatile int no_abort = 0;
-        if (last_k >= 0)
-          mbar_wait(&s.k_full[last_k % kStages], (last_k / kStages) & 1, &no_abort, p.status,
-                    TC_SITE(1, 3, last_k));
-        if (last_v >= 0)
-          mbar_wait(&s.v_full[last_v % kStages], (last_v / kStages) & 1, &no_abort, p.status,
-                    TC_SITE(1, 4, last_v));
+        if (last_kv >= 0)
+          mbar_wait(&s.kv_full[last_kv % kStages], (last_kv / kStages) & 1, &no_abort, p.status,
+                    TC_SITE(1, 3, last_kv));
       }
     }
-  } else if (warp == kMmaWarp) {
-    // ---------------------------------------------------------- MMA issuer
+  } else if (warp == kMmaWarp || warp == kMma1Warp) {
+    // ---------------------------------------------------------- MMA issuers
+    // One warp per query tile issues that tile's tcgen05.mma: S = Q K^T into
+    // its S columns, then O += P V. The tiles' products use disjoint tensor
+    // memory and their own barriers, so each tile's chain (scores, softmax,
+    // PV) runs at its own pace and the two softmax warpgroups need not do
+    // their exponentials at the same time. (A commit tracks the products of
+    // the thread that issues it.) Per key tile j the warp issues S(t, j+1)
+    // as soon as the softmax has read S(t, j), then PV(t, j).
     if (lane == 0) {
       constexpr uint32_t ab = IN_DT == WATTN_BF16 ? 1u : 0u;
       constexpr uint32_t idesc_s = idesc_f16(ab, kBM, kBN, 0, 0);  // Q, K both K-major
       constexpr uint32_t idesc_o = idesc_f16(ab, kBM, 64, 0, 1);   // P from TMEM, V MN-major
-      const uint32_t q_addr0 = smem_u32(s.q[0][0]);
-      const uint32_t k_addr0 = smem_u32(s.k[0]);
-      const uint32_t v_addr0 = smem_u32(s.v[0]);
+      // Shared-memory descriptors of the first Q, K and V tiles; a tile at
+      // byte offset off has descriptor base + off / 16 (the start-address
+      // field holds address / 16 in 14 bits, and shared addresses stay
+      // below 2^18, so the add never carries out of the field).
+      const uint64_t dq0 = smem_desc_sw128(smem_u32(s.q[0][0]), 16, 1024);
+      const uint64_t dk0 = smem_desc_sw128(smem_u32(s.k[0]), 16, 1024);
+      const uint64_t dv0 = smem_desc_sw128(smem_u32(s.v[0]), 16384, 1024);
+      constexpr uint32_t kTileDesc = kTileBytes >> 4;
+      const int t = warp == kMmaWarp ? 0 : 1;
+      const int role = 2 + 4 * t;
+      const uint32_t d_s = tmem + t * 256, d_p = d_s + 128, d_o = d_s + 192;
 
-      int qs = 0;  // Q buffer of the current chunk
-      auto issue_s = [&](int t, int st) {
-        const uint32_t qa = q_addr0 + (qs * kTiles + t) * kTileBytes, ka = k_addr0 + st * kTileBytes;
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)  // 4 x K=16 along the head dim
-          umma_ss(tmem + t * 256, smem_desc_sw128(qa + kk * 32, 16, 1024),
-                  smem_desc_sw128(ka + kk * 32, 16, 1024), idesc_s, kk > 0);
-      };
-      auto issue_pv = [&](int t, int st, bool acc) {
-        const uint32_t va = v_addr0 + st * kTileBytes;
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)  // 8 x K=16 along the keys
-          umma_ts(tmem + t * 256 + 192, tmem + t * 256 + 128 + kk * 8,
-                  smem_desc_sw128(va + kk * 2048, 16384, 1024), idesc_o, acc || kk > 0);
-      };
-
-      // Running counts per tile (barrier phases continue across units).
-      uint32_t n_s[kTiles] = {0, 0}, n_pv[kTiles] = {0, 0}, n_ep[kTiles] = {0, 0};
+      // Running counts (barrier phases continue across units).
+      uint32_t n_s = 0, n_pv = 0, n_ep = 0;
       uint32_t c = 0;  // K/V ring position
       int n_units = 0;
       bool ok = true;
-      // S(t) for key tile at ring position cs: waits until the softmax has
-      // taken the previous S of tile t into registers.
-      auto s_step = [&](const Unit &w, uint32_t cs, int j) -> bool {
+      int qs = 0;
+      // S(t) for the key tile at ring position cs.
+      auto s_step = [&](uint32_t cs, int j) -> bool {
         const int st = cs % kStages;
-        if (!mbar_wait(&s.k_full[st], (cs / kStages) & 1, abort, p.status, TC_SITE(2, 5, j)))
+        if (!mbar_wait(&s.kv_full[st], (cs / kStages) & 1, abort, p.status, TC_SITE(role, 5, j)))
           return false;
-        for (int t = 0; t < w.n_tiles; ++t) {
-          if (n_s[t] > 0 &&
-              !mbar_wait(&s.s_free[t], (n_s[t] - 1) & 1, abort, p.status, TC_SITE(2, 7 + t, j)))
-            return false;
-          tc_fence_after();
-          issue_s(t, st);
-          umma_commit(&s.s_full[t]);
-          ++n_s[t];
-        }
-        umma_commit(&s.k_empty[st]);
+        // S(t, j) overwrites S(t, j-1): the softmax must have read it.
+        if (n_s > 0 &&
+            !mbar_wait(&s.s_free[t], (n_s - 1) & 1, abort, p.status, TC_SITE(role, 7, j)))
+          return false;
+        tc_fence_after();
+        const uint64_t dq = dq0 + (uint32_t)(qs * kTiles + t) * kTileDesc;
+        const uint64_t dk = dk0 + (uint32_t)st * kTileDesc;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)  // 4 x K=16 along the head dim (32 bytes each)
+          umma_ss(d_s, dq + 2 * kk, dk + 2 * kk, idesc_s, kk > 0);
+        umma_commit(&s.s_full[t]);
+        ++n_s;
         return true;
       };
       Unit w;
       for (int kc = 0; ok && chunk_at(p, kc, w); ++kc) {
         if (w.nkv == 0) continue;
-        qs = n_units & 1;
-        if (!mbar_wait(&s.q_full[qs], (n_units >> 1) & 1, abort, p.status, TC_SITE(2, 0, n_units)))
+        qs = n_units & 1;  // Q buffer of this chunk
+        if (!mbar_wait(&s.q_full[qs], (n_units >> 1) & 1, abort, p.status,
+                       TC_SITE(role, 0, n_units)))
           break;
-        if (!s_step(w, c, 0)) break;
-        // Per key tile j: first S(t, j+1), as soon as the softmax has taken
-        // S(t, j) into registers, so the next scores are computed while the
-        // softmax works on this tile; then PV(t, j) once P(t, j) is in TMEM.
+        if (!s_step(c, 0)) break;
         for (int j = 0; j < w.nkv; ++j) {
           const uint32_t cj = c + j;
           const int st = cj % kStages;
           if (j + 1 < w.nkv) {
-            if (!s_step(w, cj + 1, j + 1)) {
+            if (!s_step(cj + 1, j + 1)) {
               ok = false;
               break;
             }
           } else {
             umma_commit(&s.q_empty[qs]);  // the chunk's last S: its Q may be replaced
           }
-          if (!mbar_wait(&s.v_full[st], (cj / kStages) & 1, abort, p.status, TC_SITE(2, 2, j))) {
+          // The unit's first PV overwrites O(t): the previous unit's
+          // epilogue must have read it.
+          if (j == 0 && n_ep > 0 &&
+              !mbar_wait(&s.o_free[t], (n_ep - 1) & 1, abort, p.status, TC_SITE(role, 9, j))) {
             ok = false;
             break;
           }
-          for (int t = 0; t < w.n_tiles; ++t) {
-            // The unit's first PV overwrites O(t): the previous unit's
-            // epilogue must have read it.
-            if (j == 0 && n_ep[t] > 0 &&
-                !mbar_wait(&s.o_free[t], (n_ep[t] - 1) & 1, abort, p.status, TC_SITE(2, 9, j))) {
-              ok = false;
-              break;
-            }
-            if (!mbar_wait(&s.p_full[t], n_pv[t] & 1, abort, p.status, TC_SITE(2, 3 + t, j))) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            issue_pv(t, st, j > 0);
-            umma_commit(&s.o_done[t]);
-            ++n_pv[t];
+          if (!mbar_wait(&s.p_full[t], n_pv & 1, abort, p.status, TC_SITE(role, 3, j))) {
+            ok = false;
+            break;
           }
-          if (!ok) break;
-          umma_commit(&s.v_empty[st]);
+          tc_fence_after();
+          const uint64_t dv = dv0 + (uint32_t)st * kTileDesc;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)  // 8 x K=16 along the keys (2048 bytes each)
+            umma_ts(d_o, d_p + kk * 8, dv + 128 * kk, idesc_o, j > 0 || kk > 0);
+          umma_commit(&s.o_done[t]);
+          ++n_pv;
         }
-        for (int t = 0; t < w.n_tiles; ++t) ++n_ep[t];
+        ++n_ep;
         c += w.nkv;
         ++n_units;
       }
-      // Drain: every MMA issued above completes before TMEM is freed. This
-      // wait ignores `abort` (it must outlive a wind-down) but stays bounded.
+      // Drain: every MMA issued above completes before TMEM is freed (the
+      // barrier completes once both warps' products are done). This wait
+      // ignores `abort` (it must outlive a wind-down) but stays bounded.
       volatile int no_abort = 0;
       umma_commit(&s.drain);
-      mbar_wait(&s.drain, 0, &no_abort, p.status, TC_SITE(2, 6, 0));
+      mbar_wait(&s.drain, 0, &no_abort, p.status, TC_SITE(role, 6, 0));
     }
   } else if (warp == kMergeWarp) {
     // ---------------------------------------------------------- split merges
@@ -571,6 +568,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t t_p = t_s + 128, t_o = t_s + 192;
     const float c = p.scale_log2;
     uint32_t n_s = 0, n_p = 0;  // S tiles read and P tiles written by this warpgroup
+    uint32_t n_ch = 0, n_st = 0;  // chunks finished / output tiles staged by this warpgroup
+    // Key tiles whose K/V stage this warpgroup has handed back (its first
+    // thread arrives once the tile's PV is seen complete).
+    uint32_t n_rel = 0;
+    auto release_kv = [&]() {
+      if (n_p > n_rel) {
+        if (wq == 0 && lane == 0) mbar_arrive(&s.kv_empty[(n_p - 1) % kStages]);
+        n_rel = n_p;
+      }
+    };
     bool ok = true;
     Unit w;
     for (int kc = 0; ok && chunk_at(p, kc, w); ++kc) {
@@ -669,6 +676,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
+          release_kv();
         }
         // O rescale for the rows whose max moved. The TMEM accesses are
         // .sync.aligned, so the whole warp takes the branch when any lane
@@ -710,6 +718,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
+      release_kv();
       uint32_t o[2][32];
       tmem_ld32(t_o, o[0]);
       tmem_ld32(t_o + 32, o[1]);
@@ -721,6 +730,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool live = qrow < p.t_q;
       OutT *dst = reinterpret_cast<OutT *>(p.o) + (int64_t)w.b * p.o_bs + (int64_t)qrow * p.o_rs +
                   w.head * kHeadDim;
+      const int qs = n_ch & 1;  // this chunk's Q buffer
+      ++n_ch;
+      const bool staged = w.n_parts() == 1 && p.tma_out;
+      // Paths that leave the Q buffer alone hand it back at once.
+      if (!staged && wq == 0 && lane == 0) mbar_arrive(&s.q_empty[qs]);
+      if (staged) {
+        // The normalised row goes into the unit's Q tile (its last S is
+        // done), 128-byte swizzled as the output map expects (16-byte chunk
+        // c of row r at chunk c ^ (r & 7)); one thread then stores the whole
+        // tile with TMA (rows past t_q fall outside the map and are not
+        // written) and hands the buffer back once the store has read it.
+        if constexpr (sizeof(OutT) == 2) {
+          uint8_t *rowp = s.q[qs][t] + row * 128;
+          const float inv = l > 0.f ? 1.f / l : 0.f;
+          auto at = [&](int i) { return __uint_as_float(o[i >> 5][i & 31]) * inv; };
+#pragma unroll
+          for (int c8 = 0; c8 < 8; ++c8) {
+            uint4 v4;
+            v4.x = pack2<OutT>(at(8 * c8 + 0), at(8 * c8 + 1));
+            v4.y = pack2<OutT>(at(8 * c8 + 2), at(8 * c8 + 3));
+            v4.z = pack2<OutT>(at(8 * c8 + 4), at(8 * c8 + 5));
+            v4.w = pack2<OutT>(at(8 * c8 + 6), at(8 * c8 + 7));
+            *reinterpret_cast<uint4 *>(rowp + ((c8 ^ (row & 7)) << 4)) = v4;
+          }
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&s.ep_full[t]);
+        if (wq == 0 && lane == 0) {
+          if (mbar_wait(&s.ep_full[t], n_st & 1, abort, p.status, TC_SITE(3 + t, 7, kc))) {
+            tma_store_4d(&map_o, s.q[qs][t], 0, w.head, w.q0 + t * kBM, w.b);
+            bulk_commit_group();
+            bulk_wait_read_all();
+          }
+          mbar_arrive(&s.q_empty[qs]);
+        }
+        ++n_st;
+        continue;
+      }
       if (w.n_parts() == 1) {
         if (live) store_row<OutT>(dst, o, l > 0.f ? 1.f / l : 0.f);
         continue;
@@ -778,7 +825,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <int IN_DT, int OUT_DT>
 int launch_typed(const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &mv,
-                 const Params &p, int batch, int n_heads, cudaStream_t stream) {
+                 const CUtensorMap &mo, const Params &p, int batch, int n_heads,
+                 cudaStream_t stream) {
   auto kern = attn_fwd_tc_kernel<IN_DT, OUT_DT>;
   const int smem = (int)sizeof(Smem) + 1024;
   // Per device and idempotent; cheap enough to repeat on every launch.
@@ -794,7 +842,8 @@ int launch_typed(const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap
   int n_ctas = std::min(p.n_units, n_sm);
   if (p.sk_tiles > 0)
     n_ctas = (int)(((long long)p.n_units * p.nkv_unit + p.sk_tiles - 1) / p.sk_tiles);
-  if (launch_pdl(kern, dim3(n_ctas), dim3(kThreads), smem, stream, mq, mk, mv, p) != cudaSuccess)
+  if (launch_pdl(kern, dim3(n_ctas), dim3(kThreads), smem, stream, mq, mk, mv, mo, p) !=
+      cudaSuccess)
     return check_launch("attn_fwd_tc (launch)");
   return check_launch("attn_fwd_tc");
 }
@@ -843,11 +892,23 @@ int launch_attn_tc(const void *q, const void *k, const void *v, void *o, int in_
                    int64_t kv_rs, int64_t o_rs, int64_t q_bs, int64_t kv_bs, int64_t o_bs,
                    float scale, int causal, int q_pos_offset, cudaStream_t stream,
                    void *split_ws, size_t split_ws_bytes) {
-  CUtensorMap mq, mk, mv;
+  CUtensorMap mq, mk, mv, mo;
   int rc;
   if ((rc = make_qkv_map(&mq, q, in_dtype, n_heads, t_q, batch, q_rs, q_bs)) != WATTN_OK) return rc;
   if ((rc = make_qkv_map(&mk, k, in_dtype, n_heads, t_kv, batch, kv_rs, kv_bs)) != WATTN_OK) return rc;
   if ((rc = make_qkv_map(&mv, v, in_dtype, n_heads, t_kv, batch, kv_rs, kv_bs)) != WATTN_OK) return rc;
+  // 16-bit output tiles leave through a TMA store (same view as Q); f32
+  // output, or an output the map cannot describe, is stored row by row.
+  int tma_out = 0;
+  mo = mq;
+  if (out_dtype != WATTN_F32) {
+    if (make_qkv_map(&mo, o, out_dtype, n_heads, t_q, batch, o_rs, o_bs) == WATTN_OK) {
+      tma_out = 1;
+    } else {
+      clear_error();
+      mo = mq;
+    }
+  }
   Params p;
   p.o = o;
   p.o_rs = o_rs;
@@ -867,6 +928,7 @@ int launch_attn_tc(const void *q, const void *k, const void *v, void *o, int in_
   p.n_units = (int)n_units;
   p.status = device_status_ptr();
   if (p.status == nullptr) return WATTN_ERR_CUDA;
+  p.tma_out = tma_out;
   // Key-tile split schedule when whole units would leave SMs idle at the end
   // (few utterances or heads per GPU).
   p.sk_tiles = 0;
@@ -901,12 +963,12 @@ int launch_attn_tc(const void *q, const void *k, const void *v, void *o, int in_
   }
   if (in_dtype == WATTN_F16) {
     if (out_dtype == WATTN_F32)
-      return launch_typed<WATTN_F16, WATTN_F32>(mq, mk, mv, p, batch, n_heads, stream);
-    return launch_typed<WATTN_F16, WATTN_F16>(mq, mk, mv, p, batch, n_heads, stream);
+      return launch_typed<WATTN_F16, WATTN_F32>(mq, mk, mv, mo, p, batch, n_heads, stream);
+    return launch_typed<WATTN_F16, WATTN_F16>(mq, mk, mv, mo, p, batch, n_heads, stream);
   }
   if (out_dtype == WATTN_F32)
-    return launch_typed<WATTN_BF16, WATTN_F32>(mq, mk, mv, p, batch, n_heads, stream);
-  return launch_typed<WATTN_BF16, WATTN_BF16>(mq, mk, mv, p, batch, n_heads, stream);
+    return launch_typed<WATTN_BF16, WATTN_F32>(mq, mk, mv, mo, p, batch, n_heads, stream);
+  return launch_typed<WATTN_BF16, WATTN_BF16>(mq, mk, mv, mo, p, batch, n_heads, stream);
 }
 
 }  // namespace wattn

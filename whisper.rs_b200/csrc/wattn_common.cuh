@@ -173,6 +173,24 @@ WATTN_DEVINL bool mbar_try_wait(uint32_t bar_addr, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking probe: whether the phase of `bar` with the given parity has
+// completed (mbarrier.test_wait never suspends the thread).
+WATTN_DEVINL bool mbar_test_wait(uint32_t bar_addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar_addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+#ifndef WATTN_WAIT_PROBE
+#define WATTN_WAIT_PROBE 1
+#endif
+
 // Waits for the phase of `bar` with the given parity to complete. Bounded:
 // if `*abort` is set (another role already gave up) it returns false at
 // once; if the wait itself runs past kWaitLimitNs it reports a timeout,
@@ -180,6 +198,7 @@ WATTN_DEVINL bool mbar_try_wait(uint32_t bar_addr, uint32_t parity) {
 WATTN_DEVINL bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort,
                             int *status, int site) {
   uint32_t addr = smem_u32(bar);
+  if (WATTN_WAIT_PROBE && mbar_test_wait(addr, parity)) return true;
   if (mbar_try_wait(addr, parity)) return true;
   unsigned long long t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
@@ -217,6 +236,27 @@ WATTN_DEVINL void tma_load_4d(void *dst, const CUtensorMap *map, uint64_t *bar, 
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
       "r"(smem_u32(bar))
       : "memory");
+}
+
+// Shared-memory tile -> global through a tensor map (elements outside the
+// map's extent are not written); completes as a bulk async-group.
+WATTN_DEVINL void tma_store_4d(const CUtensorMap *map, const void *src, int c0, int c1, int c2,
+                               int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+WATTN_DEVINL void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until every committed bulk store of this thread has read its source.
+WATTN_DEVINL void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy (TMA) accesses.
+WATTN_DEVINL void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // ------------------------------------------------------------ tcgen05
