@@ -14,17 +14,24 @@
 //   * a TMA warp streams 128-key K and V tiles through a 4-deep ring in
 //     shared memory (128-byte swizzle, the layout UMMA reads directly); the
 //     query tiles are double-buffered, so the next unit's Q is resident
-//     before the current unit ends;
-//   * an MMA warp issues tcgen05.mma: S = Q K^T (M=128, N=128, K=64) into
-//     tensor memory, then O += P V (M=128, N=64, K=128) with P read back from
-//     tensor memory. S(t, j+1) is issued as soon as the softmax has taken
-//     S(t, j) into registers, so the next scores are computed while the
-//     softmax works on the current ones;
+//     before the current unit ends. A ring stage is handed back by the two
+//     softmax warpgroups once they have seen its PV products complete;
+//   * one MMA warp per query tile issues that tile's tcgen05.mma: S = Q K^T
+//     (M=128, N=128, K=64) into tensor memory, then O += P V (M=128, N=64,
+//     K=128) with P read back from tensor memory. S(t, j+1) is issued as
+//     soon as the softmax has taken S(t, j) into registers, so the next
+//     scores are ready when the softmax finishes the current ones; the two
+//     tiles' chains do not wait on each other;
 //   * the softmax warpgroup owns one query row per thread: it reads its S
 //     row from TMEM, keeps the running max m and normaliser l in registers
 //     (exp2 domain), rescales O in TMEM only when the max grows by more than
 //     2^8 (the result is exact either way: p never exceeds 256), and writes P
-//     as packed 16-bit pairs back to TMEM.
+//     as packed 16-bit pairs back to TMEM. The two warpgroups take turns on
+//     the exponential loop, so one's loads, max and stores hide behind the
+//     other's exponentials;
+//   * a unit's 16-bit output tiles are staged in its Q buffer (free once its
+//     last scores are done) and leave with one TMA tensor store each, in
+//     place of row-by-row stores that each touch 32 rows per warp.
 //
 // When whole units would leave SMs idle at the end (few utterances or heads
 // per GPU), the units' key tiles are instead shared out evenly: each CTA
@@ -66,6 +73,7 @@ constexpr int kAttnPartFloats = 66 * kBM;  // one tile's partial: O [64][128], m
 // faster setting measured so far on B200).
 constexpr int kFmaExp2Every = 0;
 
+
 // Whether exponential pair i is computed on the FMA pipe.
 WATTN_DEVINL constexpr bool fma_exp2_slot(int i) {
   constexpr int every = kFmaExp2Every > 0 ? kFmaExp2Every : 1;
@@ -92,6 +100,9 @@ struct Smem {
   uint64_t o_done[kTiles];  // PV(t, j) complete: P(t, j+1) may be written (MMA commit)
   uint64_t o_free[kTiles];  // the epilogue has read O(t): the next unit may overwrite it
   uint64_t ep_full[kTiles];  // every row of output tile t is staged for the TMA store
+  // sfu_turn[t]: the other warpgroup has finished an exponential loop, so
+  // warpgroup t may run its next one (the turns alternate, tile 0 first).
+  uint64_t sfu_turn[kTiles];
   // Split chunks (at most two per CTA, its first two): the warpgroup's
   // partial rows of chunk i are written (all its threads; completes once).
   uint64_t part_bar[kTiles][2];
@@ -142,7 +153,12 @@ struct Params {
   float *part;
   int *cnt;
   int *status;
-  int tma_out;  // whole units' output tiles leave through map_o (16-bit output)
+  int tma_out;   // whole units' output tiles leave through map_o (16-bit output)
+  // The two softmax warpgroups take turns on the exponential loop: each
+  // one's score loads, row max, P stores and epilogue then run while the
+  // other's exponentials use the SFU (the two loops at once share it and
+  // leave it idle in between).
+  int pingpong;
 };
 
 // Normalises 64 accumulated dims by inv and stores them (16-byte stores).
@@ -364,6 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s.o_done[t], 1);
       mbar_init(&s.o_free[t], kBM);
       mbar_init(&s.ep_full[t], kBM);
+      mbar_init(&s.sfu_turn[t], kBM);
       mbar_init(&s.part_bar[t][0], kBM);
       mbar_init(&s.part_bar[t][1], kBM);
       mbar_init(&s.merge_bar[t], 1);
@@ -646,6 +663,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         // weights the tensor core multiplies V with: they then sum to
         // exactly one and the rounding error of a dominant weight cancels
         // in acc / l.
+        if (p.pingpong) {
+          // Tile 0's loop k follows tile 1's loop k-1; tile 1's loop k
+          // follows tile 0's loop k.
+          if (t == 1 || n_s > 0) {
+            const uint32_t k = t == 0 ? n_s - 1 : n_s;
+            const bool turn =
+                mbar_wait(&s.sfu_turn[t], k & 1, abort, p.status, TC_SITE(3 + t, 8, j));
+            if (!__all_sync(0xffffffffu, turn)) {
+              ok = false;
+              break;
+            }
+          }
+        }
         float2 acc2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                           make_float2(0.f, 0.f)};
         uint32_t pk[64];
@@ -665,6 +695,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         l += (acc2[0].x + acc2[0].y) + (acc2[1].x + acc2[1].y) + (acc2[2].x + acc2[2].y) +
              (acc2[3].x + acc2[3].y);
+        if (p.pingpong) mbar_arrive(&s.sfu_turn[t ^ 1]);
         // P may only overwrite the previous P once the PV reading it is
         // done (also across units), and O may only be rescaled once the
         // previous PV of this unit has added to it.
@@ -929,6 +960,7 @@ int launch_attn_tc(const void *q, const void *k, const void *v, void *o, int in_
   p.status = device_status_ptr();
   if (p.status == nullptr) return WATTN_ERR_CUDA;
   p.tma_out = tma_out;
+  p.pingpong = 1;
   // Key-tile split schedule when whole units would leave SMs idle at the end
   // (few utterances or heads per GPU).
   p.sk_tiles = 0;
@@ -956,6 +988,7 @@ int launch_attn_tc(const void *q, const void *k, const void *v, void *o, int in_
     }
     if (ws != nullptr) {
       p.sk_tiles = T;
+      p.pingpong = 0;  // measured slower under the split schedule on B200
       p.by_tiles = FastDiv::make((uint32_t)T);
       p.cnt = reinterpret_cast<int *>(ws);
       p.part = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(ws) + kCounterBytes);
