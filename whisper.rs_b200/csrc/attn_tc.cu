@@ -30,8 +30,9 @@
 //     the exponential loop, so one's loads, max and stores hide behind the
 //     other's exponentials;
 //   * a unit's 16-bit output tiles are staged in its Q buffer (free once its
-//     last scores are done) and leave with one TMA tensor store each, in
-//     place of row-by-row stores that each touch 32 rows per warp.
+//     last scores are done) and leave with one TMA tensor store each, issued
+//     by a second lane of the TMA warp, in place of row-by-row stores that
+//     each touch 32 rows per warp.
 //
 // When whole units would leave SMs idle at the end (few utterances or heads
 // per GPU), the units' key tiles are instead shared out evenly: each CTA
@@ -99,7 +100,10 @@ struct Smem {
   uint64_t p_full[kTiles];  // P(t, j) in TMEM and O(t) rescaled (softmax arrivals)
   uint64_t o_done[kTiles];  // PV(t, j) complete: P(t, j+1) may be written (MMA commit)
   uint64_t o_free[kTiles];  // the epilogue has read O(t): the next unit may overwrite it
-  uint64_t ep_full[kTiles];  // every row of output tile t is staged for the TMA store
+  // ep_full[i][t]: every row of output tile t is staged in Q buffer i for
+  // the TMA store (per buffer: a buffer is staged again only after the
+  // store lane has handed it back, so no waiter falls two phases behind).
+  uint64_t ep_full[2][kTiles];
   // sfu_turn[t]: the other warpgroup has finished an exponential loop, so
   // warpgroup t may run its next one (the turns alternate, tile 0 first).
   uint64_t sfu_turn[kTiles];
@@ -379,7 +383,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s.p_full[t], kBM);
       mbar_init(&s.o_done[t], 1);
       mbar_init(&s.o_free[t], kBM);
-      mbar_init(&s.ep_full[t], kBM);
+      mbar_init(&s.ep_full[0][t], kBM);
+      mbar_init(&s.ep_full[1][t], kBM);
       mbar_init(&s.sfu_turn[t], kBM);
       mbar_init(&s.part_bar[t][0], kBM);
       mbar_init(&s.part_bar[t][1], kBM);
@@ -450,6 +455,34 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_wait(&s.kv_full[last_kv % kStages], (last_kv / kStages) & 1, &no_abort, p.status,
                     TC_SITE(1, 3, last_kv));
       }
+    } else if (lane == 1 && p.tma_out) {
+      // ---------------------------------------------------------- output stores
+      // A whole unit's output tiles, staged by the softmax warpgroups in the
+      // unit's Q buffer, leave with one TMA tensor store each; the buffer
+      // goes back to the producer (lane 0) once the stores have read it.
+      // Split parts keep the buffer untouched and hand it back themselves.
+      uint32_t n_units = 0, n_st[2] = {0, 0};  // chunks; tiles stored from each buffer
+      bool ok = true;
+      Unit w;
+      for (int kc = 0; ok && chunk_at(p, kc, w); ++kc) {
+        if (w.nkv == 0) continue;
+        const int qs = n_units & 1;
+        ++n_units;
+        if (w.n_parts() != 1) continue;
+        for (int t = 0; t < kTiles; ++t) {
+          if (!mbar_wait(&s.ep_full[qs][t], n_st[qs] & 1, abort, p.status, TC_SITE(1, 7 + t, kc))) {
+            ok = false;
+            break;
+          }
+          tma_store_4d(&map_o, s.q[qs][t], 0, w.head, w.q0 + t * kBM, w.b);
+          bulk_commit_group();
+        }
+        bulk_wait_read_all();
+        if (!ok) break;
+        for (int t = 0; t < kTiles; ++t) mbar_arrive(&s.q_empty[qs]);
+        ++n_st[qs];
+      }
+      bulk_wait_read_all();  // the stores have read the CTA's shared memory
     }
   } else if (warp == kMmaWarp || warp == kMma1Warp) {
     // ---------------------------------------------------------- MMA issuers
@@ -585,7 +618,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t t_p = t_s + 128, t_o = t_s + 192;
     const float c = p.scale_log2;
     uint32_t n_s = 0, n_p = 0;  // S tiles read and P tiles written by this warpgroup
-    uint32_t n_ch = 0, n_st = 0;  // chunks finished / output tiles staged by this warpgroup
+    uint32_t n_ch = 0;  // chunks finished by this warpgroup
     // Key tiles whose K/V stage this warpgroup has handed back (its first
     // thread arrives once the tile's PV is seen complete).
     uint32_t n_rel = 0;
@@ -769,9 +802,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (staged) {
         // The normalised row goes into the unit's Q tile (its last S is
         // done), 128-byte swizzled as the output map expects (16-byte chunk
-        // c of row r at chunk c ^ (r & 7)); one thread then stores the whole
-        // tile with TMA (rows past t_q fall outside the map and are not
-        // written) and hands the buffer back once the store has read it.
+        // c of row r at chunk c ^ (r & 7)); the store lane of the TMA warp
+        // then stores the whole tile (rows past t_q fall outside the map and
+        // are not written) and hands the buffer back once the store has read
+        // it, while this warpgroup goes on with the next unit.
         if constexpr (sizeof(OutT) == 2) {
           uint8_t *rowp = s.q[qs][t] + row * 128;
           const float inv = l > 0.f ? 1.f / l : 0.f;
@@ -787,16 +821,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         fence_proxy_async_smem();
-        mbar_arrive(&s.ep_full[t]);
-        if (wq == 0 && lane == 0) {
-          if (mbar_wait(&s.ep_full[t], n_st & 1, abort, p.status, TC_SITE(3 + t, 7, kc))) {
-            tma_store_4d(&map_o, s.q[qs][t], 0, w.head, w.q0 + t * kBM, w.b);
-            bulk_commit_group();
-            bulk_wait_read_all();
-          }
-          mbar_arrive(&s.q_empty[qs]);
-        }
-        ++n_st;
+        mbar_arrive(&s.ep_full[qs][t]);
         continue;
       }
       if (w.n_parts() == 1) {
