@@ -161,27 +161,28 @@ def test_tc_causal_with_offset(W, oracle, t_q, t_past):
 def test_tc_strided_output_leaves_padding(W, oracle, t_q):
     # 16-bit output tiles leave through a TMA store of the whole 128-row tile:
     # rows past t_q, the padding columns of a wider row and the padding rows
-    # between utterances must keep what the caller had there.
+    # between utterances must keep what the caller had there. (f16 in and
+    # out: the same store path as bf16, with the finer f16 rounding of P.)
     import torch
     b, t_kv, h = 3, 333, 5
     w = h * 64
     o_rs, pad_rows = w + 64, 5
     o_bs = (t_q + pad_rows) * o_rs
-    qs = [rounded(randn(61 + u, t_q * w), 2) for u in range(b)]
-    ks = [rounded(randn(71 + u, t_kv * w), 2) for u in range(b)]
-    vs = [rounded(randn(81 + u, t_kv * w), 2) for u in range(b)]
+    qs = [rounded(randn(61 + u, t_q * w), 1) for u in range(b)]
+    ks = [rounded(randn(71 + u, t_kv * w), 1) for u in range(b)]
+    vs = [rounded(randn(81 + u, t_kv * w), 1) for u in range(b)]
     q = torch.cat([x[0] for x in qs])
     k = torch.cat([x[0] for x in ks])
     v = torch.cat([x[0] for x in vs])
     sentinel = 7.0
-    o = torch.full((b * o_bs,), sentinel, dtype=torch.bfloat16, device="cuda")
+    o = torch.full((b * o_bs,), sentinel, dtype=torch.float16, device="cuda")
     W.attention_fwd(q, k, v, o, batch=b, t_q=t_q, t_kv=t_kv, n_heads=h, scale=0.125,
                     o_row_stride=o_rs, o_batch_stride=o_bs)
     torch.cuda.synchronize()
     out = o.float().cpu().numpy().reshape(b, t_q + pad_rows, o_rs)
     for u in range(b):
         ref = oracle.flash_attention_2(qs[u][1], ks[u][1], vs[u][1], t_q, t_kv, h, w, False)
-        check_16bit(out[u, :t_q, :w], ref, f"strided output, utterance {u}", 2)
+        check_16bit(out[u, :t_q, :w], ref, f"strided output, utterance {u}", 1)
     assert np.all(out[:, :t_q, w:] == sentinel), "padding columns written"
     assert np.all(out[:, t_q:, :] == sentinel), "padding rows written"
 

@@ -70,9 +70,12 @@ constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 constexpr int kAttnPartFloats = 66 * kBM;  // one tile's partial: O [64][128], m [128], l [128]
 // One pair of exponentials in every kFmaExp2Every is computed on the FMA
-// pipe (exp2_fma2) instead of the SFU; 0 keeps them all on the SFU (the
-// faster setting measured so far on B200).
-constexpr int kFmaExp2Every = 0;
+// pipe (exp2_fma2) instead of the SFU (0: all on the SFU). With the two
+// warpgroups taking turns, one warp per scheduler runs the loop and leaves
+// the FMA pipe idle; one pair in 5 measured fastest on B200 (4, 6 and 8
+// within 1-4 %; one in 3 or 2 adds more instructions than it saves SFU
+// time).
+constexpr int kFmaExp2Every = 5;
 
 
 // Whether exponential pair i is computed on the FMA pipe.
