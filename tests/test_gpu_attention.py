@@ -108,18 +108,19 @@ def test_tc_large_v3_shard_of_eight(W, oracle):
 
 
 def test_attention_host_two_streams(W, oracle):
-    """wattn_attention_host (the bench's end-to-end call): 6 large-v3
-    utterances in chunks of 4 and 2 on two streams, each chunk's kernel with
-    its own split partials. Parity on one utterance of each chunk."""
+    """wattn_attention_host (the bench's end-to-end call): 5 large-v3
+    utterances in chunks of 2, 2 and 1 on two streams, each chunk's kernel
+    with its own split partials. Parity on utterances of the first and the
+    last chunk."""
     import torch
-    b, t, h = 6, 1500, 20
+    b, t, h = 5, 1500, 20
     d = h * 64
     g = torch.Generator().manual_seed(9)
     q, k, v = (torch.randn(b * t * d, generator=g).to(torch.bfloat16) for _ in range(3))
     o = torch.empty(b * t * d, dtype=torch.bfloat16)
     W.attention_host(q, k, v, o, b, t, t, h, 0.125)
     out = o.float().numpy().reshape(b, t * d)
-    for u in (1, 5):
+    for u in (1, 4):
         sl = slice(u * t * d, (u + 1) * t * d)
         ref = oracle.flash_attention_2(q[sl].float().numpy(), k[sl].float().numpy(),
                                        v[sl].float().numpy(), t, t, h, d, False)

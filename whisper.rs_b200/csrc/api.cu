@@ -433,8 +433,13 @@ int attention_host(const void *q, const void *k, const void *v, void *o, int in_
   const size_t qb = (size_t)t_q * w * es_in, kvb = (size_t)t_kv * w * es_in,
                ob = (size_t)t_q * w * es_out;
   const size_t per = round_up(qb, 256) + 2 * round_up(kvb, 256) + round_up(ob, 256);
-  // ~64 MB of device staging per stream, at least one utterance.
-  const int chunk = (int)std::max<size_t>(1, std::min<size_t>(batch, ((size_t)64 << 20) / per));
+  // ~32 MB of device staging per stream, at least one utterance: the call
+  // returns with its output written, so the first chunk's upload and the
+  // last chunk's kernel and download overlap nothing; smaller chunks shorten
+  // that, and their kernels still hide behind the uploads (measured on B200
+  // with config 3: 32 MB, two utterances, 248 ms per 32-layer step; 48 MB
+  // 253; 64 MB 264; 16 MB 281).
+  const int chunk = (int)std::max<size_t>(1, std::min<size_t>(batch, ((size_t)32 << 20) / per));
   for (int i = 0; i < 2; ++i)
     if ((rc = grow(&h->buf[i], &h->buf_bytes[i], per * chunk, false, h->st[i])) != WATTN_OK)
       return finish_host(h, rc);
