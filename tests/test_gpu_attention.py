@@ -261,6 +261,21 @@ def test_f32_tiny_encoder_shape(W, oracle):
     check_f32(host, ref, "C1 host mirror")
 
 
+@pytest.mark.parametrize("cfg", [(1, 100, 1000, 2), (2, 70, 777, 3), (1, 64, 256, 1)],
+                         ids=lambda c: "b{}_tq{}_tkv{}_h{}".format(*c))
+def test_f32_key_splits(W, oracle, cfg):
+    # Few query blocks x heads: the f32 kernel splits the keys over CTAs
+    # (ragged last key tile included) and merges the parts; still 1e-5.
+    import torch
+    b, t_q, t_kv, h = cfg
+    d = h * 64
+    q, k, v = randn(91, b * t_q * d), randn(92, b * t_kv * d), randn(93, b * t_kv * d)
+    ref = oracle.flash_attention_2_batched(q, k, v, b, t_q, t_kv, h, d, False)
+    for _ in range(2):  # the second call reuses the workspace
+        out = _run_fwd(W, *(torch.from_numpy(x).cuda() for x in (q, k, v)), 0, b, t_q, t_kv, h)
+        check_f32(out, ref, f"f32 key splits {cfg}")
+
+
 def test_single_token_and_cache_mirrors(W, oracle):
     h, d = 4, 256
     for t_kv in (1, 63, 257, 1500):

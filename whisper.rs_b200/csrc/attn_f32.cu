@@ -13,9 +13,17 @@
 // score tile (rows 4ty.., keys 8tx..) and the same block of the output
 // (rows 4ty.., dims 8tx..); the 8 threads of a row reduce with shuffles.
 // Q and K are kept d-major in shared memory so both products read float4s.
+//
+// Small problems (few query blocks x heads for the SMs, e.g. Whisper-tiny's
+// one utterance of 6 heads: 144 CTAs) split the keys: each of up to three
+// CTAs per query block walks a run of key tiles and writes its unnormalised
+// partial (64 sums, m, l per row) to a workspace, and attn_merge_f32_kernel
+// combines the parts by the same log-sum-exp rule, in f32.
 
 #include "wattn_common.cuh"
 #include "wattn_internal.h"
+
+#include <algorithm>
 
 namespace wattn {
 namespace {
@@ -29,7 +37,13 @@ struct F32Params {
   int t_q, t_kv;
   float scale_log2;
   int causal, q_pos_offset;
+  int n_splits, split_tiles;  // key splits per query block, key tiles per split
+  float *part;                // [batch][head][t_q][n_splits][kPartFloats] when split
 };
+
+// One row's partial: 64 sums, m, l, padded to 68 floats so that every row
+// starts on a 16-byte boundary (the sums are stored as float4s).
+constexpr int kPartFloats = 68;
 
 struct F32Smem {
   float qt[64][kBM + kPad];   // [d][row], pre-scaled by scale * log2(e)
@@ -48,7 +62,8 @@ __global__ void __launch_bounds__(kThreads) attn_fwd_f32_kernel(const F32Params 
 
   const int tid = threadIdx.x, ty = tid >> 3, tx = tid & 7;
   const int head = blockIdx.y, b = blockIdx.z;
-  const int q0 = blockIdx.x * kBM;
+  const int split = blockIdx.x % p.n_splits;
+  const int q0 = (blockIdx.x / p.n_splits) * kBM;
   const float *qb = p.q + (int64_t)b * p.q_bs + head * kHeadDim;
   const float *kb = p.k + (int64_t)b * p.kv_bs + head * kHeadDim;
   const float *vb = p.v + (int64_t)b * p.kv_bs + head * kHeadDim;
@@ -74,8 +89,10 @@ __global__ void __launch_bounds__(kThreads) attn_fwd_f32_kernel(const F32Params 
   }
   int kv_end = p.t_kv;
   if (p.causal) kv_end = min(kv_end, min(q0 + kBM, p.t_q) + p.q_pos_offset);
+  const int kv_beg = split * p.split_tiles * kBN;
+  if (p.n_splits > 1) kv_end = min(kv_end, kv_beg + p.split_tiles * kBN);
 
-  for (int j0 = 0; j0 < kv_end; j0 += kBN) {
+  for (int j0 = kv_beg; j0 < kv_end; j0 += kBN) {
     __syncthreads();  // previous tile fully consumed
     for (int i = 0; i < 8; ++i) {
       const int r = (tid & 31) + 32 * (i & 1), d4 = (tid >> 5) + 4 * (i >> 1);
@@ -171,6 +188,25 @@ __global__ void __launch_bounds__(kThreads) attn_fwd_f32_kernel(const F32Params 
     }
   }
 
+  if (p.n_splits > 1) {
+    // This split's partial rows: the sums unnormalised, with m and l.
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int qrow = q0 + 4 * ty + i;
+      if (qrow >= p.t_q) continue;
+      float *dst = p.part + ((((int64_t)b * gridDim.y + head) * p.t_q + qrow) * p.n_splits + split) *
+                                kPartFloats;
+      *reinterpret_cast<float4 *>(dst + 8 * tx) =
+          make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+      *reinterpret_cast<float4 *>(dst + 8 * tx + 4) =
+          make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+      if (tx == 0) {
+        dst[64] = m[i];
+        dst[65] = l[i];
+      }
+    }
+    return;
+  }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int qrow = q0 + 4 * ty + i;
@@ -182,6 +218,28 @@ __global__ void __launch_bounds__(kThreads) attn_fwd_f32_kernel(const F32Params 
     *reinterpret_cast<float4 *>(dst + 4) =
         make_float4(acc[i][4] * inv, acc[i][5] * inv, acc[i][6] * inv, acc[i][7] * inv);
   }
+}
+
+// One output row of one head from its splits' partials (64 threads, one
+// dim each): the parts' offsets m are rescaled to the largest of the parts
+// that saw keys, as the online softmax does between key tiles
+// (attention.rs:173-201), and the sum is divided by the merged normaliser.
+__global__ void __launch_bounds__(64) attn_merge_f32_kernel(const F32Params p) {
+  const int row = blockIdx.x, head = blockIdx.y, b = blockIdx.z, d = threadIdx.x;
+  const float *part =
+      p.part + (((int64_t)b * gridDim.y + head) * p.t_q + row) * p.n_splits * kPartFloats;
+  float mx = -INFINITY;
+  for (int sp = 0; sp < p.n_splits; ++sp)
+    if (part[sp * kPartFloats + 65] > 0.f) mx = fmaxf(mx, part[sp * kPartFloats + 64]);
+  float acc = 0.f, l = 0.f;
+  for (int sp = 0; sp < p.n_splits; ++sp) {
+    const float *ps = part + sp * kPartFloats;
+    if (!(ps[65] > 0.f)) continue;
+    const float w = ex2(ps[64] - mx);
+    acc = fmaf(w, ps[d], acc);
+    l = fmaf(w, ps[65], l);
+  }
+  p.o[(int64_t)b * p.o_bs + (int64_t)row * p.o_rs + head * kHeadDim + d] = l > 0.f ? acc / l : 0.f;
 }
 
 template <typename T>
@@ -214,12 +272,47 @@ int launch_attn_f32(const float *q, const float *k, const float *v, float *o, in
   p.scale_log2 = scale * 1.4426950408889634f;
   p.causal = causal;
   p.q_pos_offset = q_pos_offset;
-  dim3 grid((t_q + kBM - 1) / kBM, n_heads, batch);
+  const int n_qblk = (t_q + kBM - 1) / kBM;
+  // Key splits while the query blocks x heads fill less than half of the
+  // SMs' three resident CTAs (shared memory allows three), at least four key
+  // tiles per split; causal calls are not split.
+  int dev = 0, n_sm = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return check_launch("attn_fwd_f32: device query");
+  const long long base = (long long)n_qblk * n_heads * batch;
+  const int kv_tiles = (t_kv + kBN - 1) / kBN;
+  int n_splits = 1;
+  if (!causal && base > 0 && 2 * base <= 3LL * n_sm)
+    n_splits = (int)std::min<long long>(std::min<long long>(3, (3LL * n_sm) / base), kv_tiles / 4);
+  if (n_splits < 1) n_splits = 1;
+  p.split_tiles = (kv_tiles + n_splits - 1) / n_splits;
+  n_splits = (kv_tiles + p.split_tiles - 1) / p.split_tiles;
+  p.n_splits = std::max(n_splits, 1);
+  p.part = nullptr;
+  if (p.n_splits > 1) {
+    // The calling thread's workspace; its first kCounterBytes are the split
+    // counters of the other kernels, which stay zero between calls, so the
+    // partials go after them.
+    const size_t need = (size_t)base * kBM * p.n_splits * kPartFloats * sizeof(float);
+    uint8_t *ws = reinterpret_cast<uint8_t *>(thread_workspace(kCounterBytes + need, stream));
+    if (ws != nullptr)
+      p.part = reinterpret_cast<float *>(ws + kCounterBytes);
+    else
+      p.n_splits = 1;  // no workspace: one pass over the keys
+  }
+  dim3 grid(n_qblk * p.n_splits, n_heads, batch);
   const int smem = (int)sizeof(F32Smem);
   if (cudaFuncSetAttribute(attn_fwd_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            smem) != cudaSuccess)
     return check_launch("cudaFuncSetAttribute(attn_fwd_f32)");
   attn_fwd_f32_kernel<<<grid, kThreads, smem, stream>>>(p);
+  if (p.n_splits > 1) {
+    int rc = check_launch("attn_fwd_f32");
+    if (rc != WATTN_OK) return rc;
+    attn_merge_f32_kernel<<<dim3(t_q, n_heads, batch), 64, 0, stream>>>(p);
+    return check_launch("attn_merge_f32");
+  }
   return check_launch("attn_fwd_f32");
 }
 
