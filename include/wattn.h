@@ -212,8 +212,11 @@ int wattn_encoder_attention_residual(float *x, const float *ln_w, const float *l
  * process exits. A call whose plan needs more scratch than that returns
  * WATTN_ERR_RANGE. The first call on a device looks up the array's device
  * address (cudaGetSymbolAddress) with that device current; make that first
- * call before any stream capture. All calls on a device share the array:
- * calls whose kernels overlap on the GPU race and give wrong results. No
+ * call before any stream capture. The address is kept for the life of the
+ * process: after cudaDeviceReset on a device, do not call this entry point
+ * there again. All calls on a device share the array: calls whose kernels
+ * overlap on the GPU race and give wrong results. Arguments are checked by
+ * the same rules as wattn_decode_fwd before anything is launched. No
  * cudaMalloc, cudaFree or other allocating routine is called. */
 int wattn_decode_fwd_noalloc(const void *q, const void *k, const void *v,
                              void *o, int q_dtype, int kv_dtype,

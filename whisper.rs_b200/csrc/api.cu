@@ -537,6 +537,15 @@ int decode_host(const void *q, const void *k, const void *v, void *o, int q_dt, 
 }
 
 }  // namespace
+
+int validate_decode_args(const void *q, const void *k, const void *v, const void *o, int q_dt,
+                         int kv_dt, int out_dt, int n_groups, int group_size, int t_kv,
+                         int n_heads, int d_head, int64_t q_rs, int64_t kv_rs, int64_t kv_gs,
+                         int64_t o_rs, float scale) {
+  return validate_decode(q, k, v, o, q_dt, kv_dt, out_dt, n_groups, group_size, t_kv, n_heads,
+                         d_head, q_rs, kv_rs, kv_gs, o_rs, scale);
+}
+
 }  // namespace wattn
 
 using namespace wattn;

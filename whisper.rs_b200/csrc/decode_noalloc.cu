@@ -17,7 +17,9 @@
 // share the array and it keeps what the last call left there: the counters
 // are cleared at the start of every call, and two calls whose kernels
 // overlap on the GPU (different streams, or different host threads) race on
-// it and give wrong results.
+// it and give wrong results. The looked-up address belongs to the device's
+// current CUDA context: after cudaDeviceReset on a device this entry point
+// must not be called there again in the same process.
 
 #include <mutex>
 
@@ -69,20 +71,13 @@ extern "C" int wattn_decode_fwd_noalloc(const void *q, const void *k, const void
                                         int64_t kv_group_stride, int64_t o_row_stride,
                                         float scale, void *stream) {
   clear_error();
-  // Same argument rules as wattn_decode_fwd (checked by a call that returns
-  // before launching anything when n_groups == 0).
-  int rc = wattn_decode_fwd(q, k, v, o, q_dtype, kv_dtype, out_dtype, 0, group_size, t_kv,
-                            n_heads, d_head, q_row_stride, kv_row_stride, kv_group_stride,
-                            o_row_stride, scale, nullptr, 0, stream);
+  // The argument rules of wattn_decode_fwd, all of them (sizes, dtypes,
+  // strides, the alignment of q, k and v), checked before anything runs.
+  int rc = validate_decode_args(q, k, v, o, q_dtype, kv_dtype, out_dtype, n_groups, group_size,
+                                t_kv, n_heads, d_head, q_row_stride, kv_row_stride,
+                                kv_group_stride, o_row_stride, scale);
   if (rc != WATTN_OK) return rc;
-  if (n_groups < 0) return set_error(WATTN_ERR_INVALID, "decode_fwd_noalloc: n_groups < 0");
   if (n_groups == 0) return WATTN_OK;
-  if (!q || !o || (t_kv > 0 && (!k || !v)))
-    return set_error(WATTN_ERR_INVALID, "decode_fwd_noalloc: NULL tensor");
-  if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15)
-    return set_error(WATTN_ERR_INVALID, "decode_fwd_noalloc: k/v must be 16-byte aligned");
-  if ((int64_t)n_groups * ((group_size + 7) / 8) > 65535)
-    return set_error(WATTN_ERR_INVALID, "decode_fwd_noalloc: too many query row groups");
   cudaStream_t st = (cudaStream_t)stream;
   if (t_kv == 0)
     return launch_zero_rows(o, out_dtype, 1, n_groups * group_size, n_heads * kHeadDim,

@@ -58,6 +58,13 @@ inline CUtensorMapDataType tmap_dtype(int dt) {
 // Checks the last CUDA error after a launch; returns WATTN_OK or WATTN_ERR_CUDA.
 int check_launch(const char *what);
 
+// Argument rules of wattn_decode_fwd (sizes, dtypes, strides, alignment);
+// records the message and returns the status of the first rule broken.
+int validate_decode_args(const void *q, const void *k, const void *v, const void *o, int q_dt,
+                         int kv_dt, int out_dt, int n_groups, int group_size, int t_kv,
+                         int n_heads, int d_head, int64_t q_rs, int64_t kv_rs, int64_t kv_gs,
+                         int64_t o_rs, float scale);
+
 // ----------------------------------------------------------- kernel launchers
 // All pointers device, strides in elements; arguments already validated.
 
