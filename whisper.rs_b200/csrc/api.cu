@@ -443,14 +443,16 @@ int attention_host(const void *q, const void *k, const void *v, void *o, int in_
   for (int i = 0; i < 2; ++i)
     if ((rc = grow(&h->buf[i], &h->buf_bytes[i], per * chunk, false, h->st[i])) != WATTN_OK)
       return finish_host(h, rc);
-  // Each stream's kernels keep their key-tile split partials apart.
+  // Each stream's kernels keep their workspaces (key-tile split partials,
+  // V's f16 copy for bf16 inputs) apart.
   if (in_dt != WATTN_F32) {
     int dev = 0, n_sm = 0;
     if (cudaGetDevice(&dev) != cudaSuccess ||
         cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
       return finish_host(h, check_launch("attention_host: device query"));
     for (int i = 0; i < 2; ++i)
-      if ((rc = grow(&h->ws[i], &h->ws_bytes[i], attn_split_workspace_bytes(n_sm), true,
+      if ((rc = grow(&h->ws[i], &h->ws_bytes[i],
+                     attn_workspace_bytes(in_dt, chunk, t_kv, n_heads, n_sm), true,
                      h->st[i])) != WATTN_OK)
         return finish_host(h, rc);
   }
@@ -866,7 +868,8 @@ size_t wattn_encoder_attention_workspace_bytes(int batch, int t, int n_heads) {
   const size_t rows = (size_t)batch * t, d = (size_t)n_heads * kHeadDim;
   // fused QKV [rows][3d], the attention output [rows][d] and (for the
   // residual form) the normalised rows [rows][d], 16-bit each; then the
-  // attention's key-tile split partials (sized for the current device)
+  // attention's own workspace (key-tile split partials sized for the
+  // current device, V's f16 copy for bf16 weights)
   int dev = 0, n_sm = 0;
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
@@ -874,7 +877,7 @@ size_t wattn_encoder_attention_workspace_bytes(int batch, int t, int n_heads) {
     n_sm = 148;
   }
   return round_up(rows * 3 * d * 2, 256) + 2 * round_up(rows * d * 2, 256) +
-         round_up(attn_split_workspace_bytes(n_sm), 256);
+         round_up(attn_workspace_bytes(WATTN_BF16, batch, t, n_heads, n_sm), 256);
 }
 
 static int encoder_attention_impl(const void *x, const void *w_qkv, const float *b_qkv,

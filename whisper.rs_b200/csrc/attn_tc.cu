@@ -29,6 +29,14 @@
 //     as packed 16-bit pairs back to TMEM. The two warpgroups take turns on
 //     the exponential loop, so one's loads, max and stores hide behind the
 //     other's exponentials;
+//   * with bf16 inputs, P is rounded to f16 (11 significant bits) rather
+//     than bf16 (8), so the PV product keeps close to the reference's f32 P
+//     (attention.rs:207-222): a bandwidth-bound pre-pass writes an f16 copy
+//     of V (exact for bf16 values in f16's normal range) with the largest
+//     |v| of each block of the pass, and the kernel multiplies f16 P by that
+//     copy when the largest |v| lies in [2^-6, 65280] (values below 2^-14
+//     then err by less than 2^-25); otherwise (one uniform decision per
+//     launch) P and V stay bf16;
 //   * a unit's 16-bit output tiles are staged in its Q buffer (free once its
 //     last scores are done) and leave with one TMA tensor store each, issued
 //     by a second lane of the TMA warp, in place of row-by-row stores that
@@ -79,15 +87,16 @@ constexpr int kFmaExp2Every = 5;
 
 
 // Whether exponential pair i (of 64) is computed on the FMA pipe: one pair
-// in kFmaExp2Every, spread through the loop for bf16 inputs and the same
-// number as the loop's last pairs for f16 (the fastest placement of each
-// type measured on B200: config 3, bf16, 671 vs 624 TFLOP/s with the last
-// pairs; config 2, f16, 474 vs 424 spread out).
-template <int IN_DT>
+// in kFmaExp2Every, spread through the loop when P is bf16 and the same
+// number as the loop's last pairs when P is f16 (the fastest placement of
+// each P type measured on B200: bf16 P, config 3, 671 vs 624 TFLOP/s with
+// the last pairs; f16 P, config 2, 474 vs 424 spread out, and config 3 with
+// bf16 inputs, 666 vs 571).
+template <int P_DT>
 WATTN_DEVINL constexpr bool fma_exp2_slot(int i) {
   constexpr int every = kFmaExp2Every > 0 ? kFmaExp2Every : 1;
   constexpr int n_fma = kFmaExp2Every > 0 ? 64 / every : 0;
-  if constexpr (IN_DT == WATTN_F16) return i >= 64 - n_fma;
+  if constexpr (P_DT == WATTN_F16) return i >= 64 - n_fma;
   return kFmaExp2Every > 0 && i % every == every - 1;
 }
 
@@ -173,6 +182,11 @@ struct Params {
   // other's exponentials use the SFU (the two loops at once share it and
   // leave it idle in between).
   int pingpong;
+  // bf16 inputs: the largest |v| of each block of the V pre-pass
+  // (vmax[0..vmax_n), f32 bits) and the launch's gate: 0 none; 1 run only
+  // when V fits f16 faithfully; 2 run only when it does not.
+  const uint32_t *vmax;
+  int vmax_n, gate;
 };
 
 // Normalises 64 accumulated dims by inv and stores them (16-byte stores).
@@ -364,63 +378,15 @@ WATTN_DEVINL void merge_row(const Params &p, const Unit &w, int t, int row, OutT
   }
 }
 
-template <int IN_DT, int OUT_DT>
-__global__ void __launch_bounds__(kThreads, 1)
-    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_q,
-                       const __grid_constant__ CUtensorMap map_k,
-                       const __grid_constant__ CUtensorMap map_v,
-                       const __grid_constant__ CUtensorMap map_o, const Params p) {
-  using InT = typename Elem<IN_DT>::T;
+// The roles of one CTA (TMA producer and store lane, MMA warps, merge warp,
+// softmax warpgroups) over its work units, with P rounded to PV_DT and
+// map_v viewing V in that type.
+template <int IN_DT, int PV_DT, int OUT_DT>
+WATTN_DEVINL void attn_roles(const CUtensorMap &map_q, const CUtensorMap &map_k,
+                             const CUtensorMap &map_v, const CUtensorMap &map_o, const Params &p,
+                             Smem &s, uint32_t tmem, volatile int *abort, int warp, int lane) {
+  using PT = typename Elem<PV_DT>::T;  // the type P is rounded to (that of V)
   using OutT = typename Elem<OUT_DT>::T;
-  extern __shared__ uint8_t smem_raw[];
-  Smem &s = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                      ~uintptr_t(1023));
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s.q_full[i], 1);
-      // a commit from each tile's MMA warp and an arrival from each epilogue
-      mbar_init(&s.q_empty[i], 2 * kTiles);
-    }
-    for (int i = 0; i < kStages; ++i) {
-      mbar_init(&s.kv_full[i], 1);
-      mbar_init(&s.kv_empty[i], kTiles);
-    }
-    for (int t = 0; t < kTiles; ++t) {
-      mbar_init(&s.s_full[t], 1);
-      mbar_init(&s.s_free[t], kBM);
-      mbar_init(&s.p_full[t], kBM);
-      mbar_init(&s.o_done[t], 1);
-      mbar_init(&s.o_free[t], kBM);
-      mbar_init(&s.ep_full[0][t], kBM);
-      mbar_init(&s.ep_full[1][t], kBM);
-      mbar_init(&s.sfu_turn[t], kBM);
-      mbar_init(&s.part_bar[t][0], kBM);
-      mbar_init(&s.part_bar[t][1], kBM);
-      mbar_init(&s.merge_bar[t], 1);
-    }
-    mbar_init(&s.drain, kTiles);  // one commit from each MMA warp
-    s.abort = 0;
-    fence_barrier_init();
-  }
-  if (warp == kMmaWarp) {
-    __syncwarp();
-    tmem_alloc(&s.tmem_base, kTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  // The set-up above overlaps the end of the previous kernel in the stream
-  // (launched with programmatic serialisation); global memory is read and
-  // written only after it has completed. The next launch may start its own
-  // set-up as this grid's CTAs retire.
-  grid_dep_wait();
-  grid_dep_launch();
-  const uint32_t tmem = s.tmem_base;
-  volatile int *abort = &s.abort;
-
   if (warp == kTmaWarp) {
     // ---------------------------------------------------------- TMA producer
     if (lane == 0) {
@@ -506,7 +472,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t ab = IN_DT == WATTN_BF16 ? 1u : 0u;
       constexpr uint32_t idesc_s = idesc_f16(ab, kBM, kBN, 0, 0);  // Q, K both K-major
-      constexpr uint32_t idesc_o = idesc_f16(ab, kBM, 64, 0, 1);   // P from TMEM, V MN-major
+      constexpr uint32_t idesc_o =  // P from TMEM, V MN-major, both of V's type
+          idesc_f16(PV_DT == WATTN_BF16 ? 1u : 0u, kBM, 64, 0, 1);
       // Shared-memory descriptors of the first Q, K and V tiles; a tile at
       // byte offset off has descriptor base + off / 16 (the start-address
       // field holds address / 16 in 14 bits, and shared addresses stay
@@ -726,15 +693,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 64; ++i) {
           const float2 x = __ffma2_rn(make_float2(sv[2 * i], sv[2 * i + 1]), c2, nmu2);
           float2 pv;
-          if (fma_exp2_slot<IN_DT>(i)) {
+          if (fma_exp2_slot<PV_DT>(i)) {
             pv = exp2_fma2(x);
           } else {
             pv.x = ex2(x.x);
             pv.y = ex2(x.y);
           }
-          const uint32_t wd = pack2<InT>(pv.x, pv.y);
+          const uint32_t wd = pack2<PT>(pv.x, pv.y);
           pk[i] = wd;
-          acc2[i & 3] = __fadd2_rn(acc2[i & 3], unpack2<InT>(wd));
+          acc2[i & 3] = __fadd2_rn(acc2[i & 3], unpack2<PT>(wd));
         }
         l += (acc2[0].x + acc2[0].y) + (acc2[1].x + acc2[1].y) + (acc2[2].x + acc2[2].y) +
              (acc2[3].x + acc2[3].y);
@@ -879,6 +846,89 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+}
+
+// map_v views V in PV_DT: the caller's V, or (bf16 inputs, PV_DT f16) its
+// f16 copy.
+template <int IN_DT, int PV_DT, int OUT_DT>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_q,
+                       const __grid_constant__ CUtensorMap map_k,
+                       const __grid_constant__ CUtensorMap map_v,
+                       const __grid_constant__ CUtensorMap map_o, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem &s = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                      ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.q_full[i], 1);
+      // a commit from each tile's MMA warp and an arrival from each epilogue
+      mbar_init(&s.q_empty[i], 2 * kTiles);
+    }
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&s.kv_full[i], 1);
+      mbar_init(&s.kv_empty[i], kTiles);
+    }
+    for (int t = 0; t < kTiles; ++t) {
+      mbar_init(&s.s_full[t], 1);
+      mbar_init(&s.s_free[t], kBM);
+      mbar_init(&s.p_full[t], kBM);
+      mbar_init(&s.o_done[t], 1);
+      mbar_init(&s.o_free[t], kBM);
+      mbar_init(&s.ep_full[0][t], kBM);
+      mbar_init(&s.ep_full[1][t], kBM);
+      mbar_init(&s.sfu_turn[t], kBM);
+      mbar_init(&s.part_bar[t][0], kBM);
+      mbar_init(&s.part_bar[t][1], kBM);
+      mbar_init(&s.merge_bar[t], 1);
+    }
+    mbar_init(&s.drain, kTiles);  // one commit from each MMA warp
+    s.abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == kMmaWarp) {
+    __syncwarp();
+    tmem_alloc(&s.tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  // The set-up above overlaps the end of the previous kernel in the stream
+  // (launched with programmatic serialisation); global memory is read and
+  // written only after it has completed. The next launch may start its own
+  // set-up as this grid's CTAs retire.
+  grid_dep_wait();
+  grid_dep_launch();
+  // bf16 inputs: two launches follow the V pre-pass, one per type of P and
+  // V; the gate (a uniform decision on the pre-pass's block maxima) lets the
+  // f16 one run when every block's largest |v| lies within f16's faithful
+  // range, the bf16 one otherwise. A launch that does not run frees its
+  // tensor memory and returns.
+  if (p.gate != 0) {
+    bool big = false, some = false;  // a block's largest |v| beyond f16 / at least 2^-6
+    for (int i = threadIdx.x; i < p.vmax_n; i += kThreads) {
+      const float m = __uint_as_float(__ldcg(p.vmax + i));
+      big = big || !(m <= 65280.0f);
+      some = some || m >= 0.015625f;
+    }
+    const bool fits = !__syncthreads_or(big) && __syncthreads_or(some);
+    if (fits != (p.gate == 1)) {
+      tc_fence_before();
+      __syncthreads();
+      if (warp == kMmaWarp) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(s.tmem_base, kTmemCols);
+      }
+      return;
+    }
+  }
+  const uint32_t tmem = s.tmem_base;
+  attn_roles<IN_DT, PV_DT, OUT_DT>(map_q, map_k, map_v, map_o, p, s, tmem, &s.abort, warp, lane);
+
   // Teardown: after the last TMEM access of every warp, free the columns.
   tc_fence_before();
   __syncthreads();
@@ -889,11 +939,56 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int IN_DT, int OUT_DT>
+// ---------------------------------------------------------------- V pre-pass
+// bf16 inputs: V is copied to f16, contiguous [batch][t_kv][width], by a
+// bandwidth-bound pass (each warp converts one row at a time, 16 bytes per
+// lane, so a warp reads and writes 512 contiguous bytes); every block also
+// writes its largest |v| (f32 bits) to vmax[blockIdx.x], the attention
+// launches' gate. A NaN is passed over (it stays NaN in f16 as in bf16).
+constexpr int kVConvThreads = 256;
+constexpr int kVConvMaxBlocks = 1024;
+
+__global__ void __launch_bounds__(kVConvThreads)
+    v_to_f16_kernel(const uint4 *__restrict__ v, int64_t rs16, int64_t bs16, int t_kv, int rows,
+                    int cpr, uint4 *__restrict__ out, uint32_t *__restrict__ vmax) {
+  grid_dep_wait();
+  grid_dep_launch();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int kWarps = kVConvThreads / 32;
+  float mx = 0.f;
+  for (int r = blockIdx.x * kWarps + warp; r < rows; r += gridDim.x * kWarps) {
+    const int b = r / t_kv, t = r - b * t_kv;
+    const uint4 *src = v + b * bs16 + t * rs16;
+    uint4 *dst = out + (int64_t)r * cpr;
+#pragma unroll 4
+    for (int c = lane; c < cpr; c += 32) {
+      uint4 x = __ldcs(src + c);
+      uint32_t *wd = reinterpret_cast<uint32_t *>(&x);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float lo = __uint_as_float(wd[e] << 16), hi = __uint_as_float(wd[e] & 0xffff0000u);
+        mx = fmax3(mx, fabsf(lo), fabsf(hi));
+        wd[e] = pack2<__half>(lo, hi);
+      }
+      dst[c] = x;
+    }
+  }
+  __shared__ uint32_t wmax[kWarps];
+  const uint32_t m = __reduce_max_sync(0xffffffffu, __float_as_uint(mx));
+  if (lane == 0) wmax[warp] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t bm = 0;
+#pragma unroll
+    for (int i = 0; i < kWarps; ++i) bm = max(bm, wmax[i]);
+    vmax[blockIdx.x] = bm;
+  }
+}
+
+template <int IN_DT, int PV_DT, int OUT_DT>
 int launch_typed(const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &mv,
-                 const CUtensorMap &mo, const Params &p, int batch, int n_heads,
-                 cudaStream_t stream) {
-  auto kern = attn_fwd_tc_kernel<IN_DT, OUT_DT>;
+                 const CUtensorMap &mo, const Params &p, cudaStream_t stream) {
+  auto kern = attn_fwd_tc_kernel<IN_DT, PV_DT, OUT_DT>;
   const int smem = (int)sizeof(Smem) + 1024;
   // Per device and idempotent; cheap enough to repeat on every launch.
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
@@ -953,12 +1048,23 @@ size_t attn_split_workspace_bytes(int n_sm) {
   return kCounterBytes + (size_t)2 * n_sm * kTiles * kAttnPartFloats * sizeof(float);
 }
 
+// [split counters and partials][bf16 inputs: V's f16 copy][its block maxima]
+static size_t v_copy_offset(int n_sm) { return round_up_256(attn_split_workspace_bytes(n_sm)); }
+
+size_t attn_workspace_bytes(int in_dtype, int batch, int t_kv, int n_heads, int n_sm) {
+  size_t n = v_copy_offset(n_sm);
+  if (in_dtype == WATTN_BF16)
+    n += round_up_256((size_t)batch * t_kv * n_heads * kHeadDim * 2) +
+         kVConvMaxBlocks * sizeof(uint32_t);
+  return n;
+}
+
 int launch_attn_tc(const void *q, const void *k, const void *v, void *o, int in_dtype,
                    int out_dtype, int batch, int t_q, int t_kv, int n_heads, int64_t q_rs,
                    int64_t kv_rs, int64_t o_rs, int64_t q_bs, int64_t kv_bs, int64_t o_bs,
                    float scale, int causal, int q_pos_offset, cudaStream_t stream,
                    void *split_ws, size_t split_ws_bytes) {
-  CUtensorMap mq, mk, mv, mo;
+  CUtensorMap mq, mk, mv, mo, mv16;
   int rc;
   if ((rc = make_qkv_map(&mq, q, in_dtype, n_heads, t_q, batch, q_rs, q_bs)) != WATTN_OK) return rc;
   if ((rc = make_qkv_map(&mk, k, in_dtype, n_heads, t_kv, batch, kv_rs, kv_bs)) != WATTN_OK) return rc;
@@ -1004,21 +1110,40 @@ int launch_attn_tc(const void *q, const void *k, const void *v, void *o, int in_
   p.by_nkv = FastDiv::make((uint32_t)p.nkv_unit);
   p.part = nullptr;
   p.cnt = nullptr;
+  p.vmax = nullptr;
+  p.vmax_n = 0;
+  p.gate = 0;
   int dev = 0, n_sm = 0;
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return check_launch("attn_fwd_tc: device query");
+  // bf16 inputs need the workspace for V's f16 copy: the caller's, which
+  // must then hold it, or the calling thread's.
+  const bool conv_v = in_dtype == WATTN_BF16;
+  const size_t ws_need = attn_workspace_bytes(in_dtype, batch, t_kv, n_heads, n_sm);
+  uint8_t *wsb = reinterpret_cast<uint8_t *>(split_ws);
+  if (conv_v) {
+    if (wsb != nullptr && split_ws_bytes < ws_need)
+      return set_error(WATTN_ERR_INVALID,
+                       "attention: a workspace of %zu bytes is needed for bf16 inputs (%zu given)",
+                       ws_need, split_ws_bytes);
+    if (wsb == nullptr) {
+      wsb = reinterpret_cast<uint8_t *>(thread_workspace(ws_need, stream));
+      if (wsb == nullptr) return set_error(WATTN_ERR_NOMEM, "attention workspace allocation failed");
+    }
+  }
   const int T = plan_attn_split(n_units, p.nkv_unit, n_sm, causal);
   if (T > 0) {
     const long long n_ctas = ((long long)n_units * p.nkv_unit + T - 1) / T;
     const size_t need = attn_split_workspace_bytes((int)n_ctas);
-    void *ws = split_ws;
-    if (ws != nullptr && split_ws_bytes < need) ws = nullptr;  // too small: whole units
-    if (ws != nullptr) {
+    void *ws = wsb;
+    if (ws != nullptr && split_ws != nullptr && split_ws_bytes < need)
+      ws = nullptr;  // too small: whole units
+    if (ws != nullptr && split_ws != nullptr) {
       // a caller's buffer: the counters this launch uses start at zero
       if (cudaMemsetAsync(ws, 0, (size_t)n_ctas * kTiles * sizeof(int), stream) != cudaSuccess)
         return check_launch("attn_fwd_tc: counter reset");
-    } else if (split_ws == nullptr) {
+    } else if (ws == nullptr && split_ws == nullptr) {
       ws = thread_workspace(need, stream);
     }
     if (ws != nullptr) {
@@ -1031,12 +1156,41 @@ int launch_attn_tc(const void *q, const void *k, const void *v, void *o, int in_
   }
   if (in_dtype == WATTN_F16) {
     if (out_dtype == WATTN_F32)
-      return launch_typed<WATTN_F16, WATTN_F32>(mq, mk, mv, mo, p, batch, n_heads, stream);
-    return launch_typed<WATTN_F16, WATTN_F16>(mq, mk, mv, mo, p, batch, n_heads, stream);
+      return launch_typed<WATTN_F16, WATTN_F16, WATTN_F32>(mq, mk, mv, mo, p, stream);
+    return launch_typed<WATTN_F16, WATTN_F16, WATTN_F16>(mq, mk, mv, mo, p, stream);
   }
-  if (out_dtype == WATTN_F32)
-    return launch_typed<WATTN_BF16, WATTN_F32>(mq, mk, mv, mo, p, batch, n_heads, stream);
-  return launch_typed<WATTN_BF16, WATTN_BF16>(mq, mk, mv, mo, p, batch, n_heads, stream);
+  // bf16: V's f16 copy and its block maxima, then the two gated launches:
+  // the bf16 one first (it finds nothing to do in the usual case, and its
+  // set-up overlaps the pre-pass's end), then the f16 one.
+  const long long rows = (long long)batch * t_kv;
+  if (rows > INT_MAX) return set_error(WATTN_ERR_INVALID, "attention: batch * t_kv exceeds 2^31");
+  const int width = n_heads * kHeadDim;
+  uint8_t *v16 = wsb + v_copy_offset(n_sm);
+  uint32_t *vmax = reinterpret_cast<uint32_t *>(v16 + round_up_256((size_t)rows * width * 2));
+  const int n_blk = (int)std::min<long long>(
+      std::min<long long>(kVConvMaxBlocks, (long long)n_sm * (2048 / kVConvThreads)),
+      (rows + kVConvThreads / 32 - 1) / (kVConvThreads / 32));
+  if (launch_pdl(v_to_f16_kernel, dim3(n_blk), dim3(kVConvThreads), 0, stream,
+                 reinterpret_cast<const uint4 *>(v), (int64_t)(kv_rs / 8),
+                 (int64_t)(batch > 1 ? kv_bs / 8 : 0), t_kv, (int)rows, width / 8,
+                 reinterpret_cast<uint4 *>(v16), vmax) != cudaSuccess)
+    return check_launch("v_to_f16 (launch)");
+  if ((rc = make_qkv_map(&mv16, v16, WATTN_F16, n_heads, t_kv, batch, width,
+                         (int64_t)t_kv * width)) != WATTN_OK)
+    return rc;
+  p.vmax = vmax;
+  p.vmax_n = n_blk;
+  Params pb = p;
+  pb.gate = 2;
+  p.gate = 1;
+  if (out_dtype == WATTN_F32) {
+    rc = launch_typed<WATTN_BF16, WATTN_BF16, WATTN_F32>(mq, mk, mv, mo, pb, stream);
+    if (rc == WATTN_OK) rc = launch_typed<WATTN_BF16, WATTN_F16, WATTN_F32>(mq, mk, mv16, mo, p, stream);
+    return rc;
+  }
+  rc = launch_typed<WATTN_BF16, WATTN_BF16, WATTN_BF16>(mq, mk, mv, mo, pb, stream);
+  if (rc == WATTN_OK) rc = launch_typed<WATTN_BF16, WATTN_F16, WATTN_BF16>(mq, mk, mv16, mo, p, stream);
+  return rc;
 }
 
 }  // namespace wattn

@@ -75,11 +75,15 @@ int validate_decode_args(const void *q, const void *k, const void *v, const void
 constexpr int kMaxSplitCounters = 65536;
 constexpr size_t kCounterBytes = (size_t)kMaxSplitCounters * sizeof(int);
 
-// tcgen05 tensor-core attention, 16-bit inputs (attn_tc.cu). When the
-// key-tile split schedule is chosen, its partials go to split_ws (a caller's
-// buffer of split_ws_bytes whose counters this call zeroes first) or, with
-// split_ws NULL, to the calling thread's workspace; without room for them
-// whole units are dealt round-robin.
+inline size_t round_up_256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// tcgen05 tensor-core attention, 16-bit inputs (attn_tc.cu). Its workspace
+// (split_ws: a caller's 256-byte aligned buffer of split_ws_bytes, or, with
+// split_ws NULL, the calling thread's) holds the key-tile split schedule's
+// counters and partials (this call zeroes the counters it uses in a
+// caller's buffer; without room for the partials whole units are dealt
+// round-robin) and, for bf16 inputs, V's f16 copy with its block maxima,
+// for which a caller's buffer must have attn_workspace_bytes() bytes.
 int launch_attn_tc(const void *q, const void *k, const void *v, void *o, int in_dtype,
                    int out_dtype, int batch, int t_q, int t_kv, int n_heads, int64_t q_rs,
                    int64_t kv_rs, int64_t o_rs, int64_t q_bs, int64_t kv_bs, int64_t o_bs,
@@ -90,6 +94,8 @@ int launch_attn_tc(const void *q, const void *k, const void *v, void *o, int in_
 int plan_attn_split(long long n_units, int nkv, int n_sm, int causal);
 // Workspace of the split schedule on a device of n_sm SMs (its upper bound).
 size_t attn_split_workspace_bytes(int n_sm);
+// Whole workspace of one launch_attn_tc call on a device of n_sm SMs.
+size_t attn_workspace_bytes(int in_dtype, int batch, int t_kv, int n_heads, int n_sm);
 
 // f32 CUDA-core attention (attn_f32.cu).
 int launch_attn_f32(const float *q, const float *k, const float *v, float *o, int batch,
