@@ -251,6 +251,7 @@ def bench_encoder(W, rank, world, steps, warmup, e2e_steps):
             host.append(tuple(x.cpu().pin_memory() for x in (q, k, v)) +
                         (torch.empty(n, dtype=torch.bfloat16).pin_memory(),))
         W.attention_host(*host[0], bl, T, T, H, 0.125)  # warm the host path
+        h2d_gbs = h2d_bandwidth(host[0][0], world)
         barrier(world)
         t0 = time.perf_counter()
         for s in range(e2e_steps):
@@ -264,13 +265,38 @@ def bench_encoder(W, rank, world, steps, warmup, e2e_steps):
                "h2d_bytes_per_step": sum_over_ranks(h2d, world),
                "d2h_bytes_per_step": sum_over_ranks(n * 2 * L, world),
                "steps": e2e_steps, "ms_per_step": e2e_ms / e2e_steps,
-               "path": "wattn_attention_host (pinned host buffers, chunked H2D/kernel/D2H on 2 streams)"}
+               "path": "wattn_attention_host (pinned host buffers, chunked H2D/kernel/D2H on 2 streams)",
+               "h2d_copy_gbs": h2d_gbs}
         del host
     del layers
     torch.cuda.empty_cache()
+    # Each bf16 call is three kernels: V's f16 copy, the bf16-P attention
+    # (which finds nothing to do unless V exceeds f16) and the f16-P one.
     return {"value": value, "ms": ms, "achieved": achieved, "avg_launch_ms": avg_launch_ms,
-            "launches": steps * L, "clocks": clk.summary(), "e2e": e2e,
+            "launches": 3 * steps * L, "clocks": clk.summary(), "e2e": e2e,
             "flops_per_launch": flops_layer_local, "local_batch": bl}
+
+
+def h2d_bandwidth(src, world: int, reps: int = 8) -> dict:
+    """Pinned host -> device copy bandwidth with every rank copying at once
+    (the e2e path's floor): per rank (slowest rank) and summed over ranks."""
+    import torch
+    dst = torch.empty_like(src, device="cuda")
+    stream = torch.cuda.current_stream()
+    dst.copy_(src, non_blocking=True)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        dst.copy_(src, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    nbytes = src.numel() * src.element_size() * reps
+    barrier(world)
+    del dst
+    return {"per_rank": nbytes / (ms * 1e-3) / 1e9, "all_ranks": nbytes * world / (ms * 1e-3) / 1e9,
+            "bytes_per_rank": nbytes}
 
 
 # --------------------------------------------------------------------- decode (C4, C5)
@@ -561,7 +587,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["wattn", "reference"], default="wattn")
-    ap.add_argument("--e2e-steps", type=int, default=1)
+    ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-extras", action="store_true", help="headline only")
     ap.add_argument("--only", choices=["all", "enc", "dec", "xdec", "proj", "block"], default="all",
@@ -648,30 +674,34 @@ def main():
                                            if peaks.get("bf16_tflops_sustained") else None),
                      "flops_per_launch": enc["flops_per_launch"],
                      "avg_launch_ms": enc["avg_launch_ms"],
+                     "timed": "each attention call: V's f16 pre-pass and the gated launches",
                      "traffic": traffic},
         "gpu_launches": enc["launches"],
         "clocks": enc["clocks"],
         "e2e": enc["e2e"],
         "cpu_baseline": cb,
     }
+    # The decode workloads go last in the line (compact), so that a display
+    # of the line's end still shows them at every N.
+    if also:
+        line["also"] = also
     if dec:
         line["decode"] = {"config": "c5_turbo_self_paged_plus_cross", "value": dec["value"],
                           "unit": "GB/s", "frac_of_hbm": dec["value"] / (peaks["hbm_gbs"] * world),
-                          "ms": dec["ms"], "launches": dec["launches"],
+                          "n_gpus": world, "ms": dec["ms"], "launches": dec["launches"],
                           "mean_cache_len": dec["mean_cache_len"],
                           "paged_kernel_traffic": load_traffic().get("decode_stream_paged_c5_layer")}
     if xdec:
         line["cross_decode"] = {"config": "c4_large_v3_cross", "value": xdec["value"],
                                 "unit": "GB/s",
+                                "frac_of_hbm": xdec["value"] / (peaks["hbm_gbs"] * world),
+                                "n_gpus": world, "ms": xdec["ms"], "launches": xdec["launches"],
                                 "roofline": {"bound": "hbm", "kernel": "decode_stream_dense",
                                              "achieved": xdec["achieved"], "peak": peaks["hbm_gbs"],
                                              "unit": "GB/s",
                                              "frac": xdec["achieved"] / peaks["hbm_gbs"],
                                              "bytes_per_launch": xdec["bytes_per_launch"],
-                                             "traffic": load_traffic().get("decode_stream_dense_c4_layer")},
-                                "ms": xdec["ms"], "launches": xdec["launches"]}
-    if also:
-        line["also"] = also
+                                             "traffic": load_traffic().get("decode_stream_dense_c4_layer")}}
     print(json.dumps(line))
 
 
