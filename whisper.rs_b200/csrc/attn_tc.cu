@@ -669,10 +669,13 @@ WATTN_DEVINL void attn_roles(const CUtensorMap &map_q, const CUtensorMap &map_k,
         const float mu = (m == -INFINITY) ? 0.f : m;
         const float2 c2 = make_float2(c, c), nmu2 = make_float2(-mu, -mu);
         // P = 2^(s*c - mu), packed to 16-bit pairs (kept in registers until
-        // the previous PV is done, then stored to TMEM). l sums the *rounded*
-        // weights the tensor core multiplies V with: they then sum to
-        // exactly one and the rounding error of a dominant weight cancels
-        // in acc / l.
+        // the previous PV is done, then stored to TMEM). With bf16 P, l sums
+        // the *rounded* weights the tensor core multiplies V with: they then
+        // sum to exactly one and the rounding error of a dominant weight
+        // cancels in acc / l. With f16 P (2^-12 relative rounding), l sums
+        // the f32 weights: widening packed f16 back to f32 costs more than
+        // the exponentials on B200, and the normaliser then differs from the
+        // rounded weights' sum by at most 2^-12 relative.
         if (p.pingpong) {
           // Tile 0's loop k follows tile 1's loop k-1; tile 1's loop k
           // follows tile 0's loop k.
@@ -701,7 +704,10 @@ WATTN_DEVINL void attn_roles(const CUtensorMap &map_q, const CUtensorMap &map_k,
           }
           const uint32_t wd = pack2<PT>(pv.x, pv.y);
           pk[i] = wd;
-          acc2[i & 3] = __fadd2_rn(acc2[i & 3], unpack2<PT>(wd));
+          if constexpr (PV_DT == WATTN_F16)
+            acc2[i & 3] = __fadd2_rn(acc2[i & 3], pv);
+          else
+            acc2[i & 3] = __fadd2_rn(acc2[i & 3], unpack2<PT>(wd));
         }
         l += (acc2[0].x + acc2[0].y) + (acc2[1].x + acc2[1].y) + (acc2[2].x + acc2[2].y) +
              (acc2[3].x + acc2[3].y);
