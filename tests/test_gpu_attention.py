@@ -231,6 +231,25 @@ def test_tc_bf16_v_tiles_outside_f16_range(W, oracle, scale_exp):
     assert cosine(out, ref) > 0.9999
 
 
+@pytest.mark.parametrize("dt", [1, 2], ids=["f16", "bf16"])
+def test_tc_later_key_tile_with_far_larger_scores(W, oracle, dt):
+    """Key tiles after a chunk's first are weighted at the running offset and
+    find their own row max on the way; a tile whose scores lie far above it
+    (keys 256..383 scaled by 20 here: score jumps of hundreds) is computed
+    again with its max. Rows see that tile dominate; the result must still
+    match the oracle."""
+    b, t_q, t_kv, h = 1, 300, 700, 3
+    d = h * 64
+    q = randn(801, t_q * d)
+    k = randn(802, t_kv * d).reshape(t_kv, d)
+    k[256:384] *= np.float32(20.0)
+    v = randn(803, t_kv * d)
+    (qd, qf), (kd, kf), (vd, vf) = rounded(q, dt), rounded(k.ravel(), dt), rounded(v, dt)
+    ref = oracle.flash_attention_2_batched(qf, kf, vf, b, t_q, t_kv, h, d, False)
+    out = _run_fwd(W, qd, kd, vd, 0, b, t_q, t_kv, h)
+    check_16bit(out, ref, f"dt={dt} far larger later scores")
+
+
 def test_tc_output_fully_overwritten(W, oracle):
     # test_flash_attention_tiled.rs:243-263: NaN-prefilled output, causal, ragged.
     import torch
