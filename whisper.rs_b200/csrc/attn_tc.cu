@@ -27,7 +27,8 @@
 //     (exp2 domain), rescales O in TMEM only when the max grows by more than
 //     2^8 (the result is exact either way: p never exceeds 256), and writes P
 //     as packed 16-bit pairs back to TMEM. The two warpgroups take turns on
-//     the exponential loop, so one's loads, max and stores hide behind the
+//     the exponential loop, warp by warp on each scheduler (whose SFU the
+//     two warps share), so one's loads, max and stores hide behind the
 //     other's exponentials;
 //   * with bf16 inputs, P is rounded to f16 (11 significant bits) rather
 //     than bf16 (8), so the PV product keeps close to the reference's f32 P
@@ -123,9 +124,11 @@ struct Smem {
   // the TMA store (per buffer: a buffer is staged again only after the
   // store lane has handed it back, so no waiter falls two phases behind).
   uint64_t ep_full[2][kTiles];
-  // sfu_turn[t]: the other warpgroup has finished an exponential loop, so
+  // sfu_turn[t][w]: warp w of the other warpgroup (on the same scheduler,
+  // so the same SFU) has finished an exponential loop, so warp w of
   // warpgroup t may run its next one (the turns alternate, tile 0 first).
-  uint64_t sfu_turn[kTiles];
+  // Per scheduler, a warp need not wait for the slowest of the other four.
+  uint64_t sfu_turn[kTiles][4];
   // Split chunks (at most two per CTA, its first two): the warpgroup's
   // partial rows of chunk i are written (all its threads; completes once).
   uint64_t part_bar[kTiles][2];
@@ -682,7 +685,7 @@ WATTN_DEVINL void attn_roles(const CUtensorMap &map_q, const CUtensorMap &map_k,
           if (t == 1 || n_s > 0) {
             const uint32_t k = t == 0 ? n_s - 1 : n_s;
             const bool turn =
-                mbar_wait(&s.sfu_turn[t], k & 1, abort, p.status, TC_SITE(3 + t, 8, j));
+                mbar_wait(&s.sfu_turn[t][wq], k & 1, abort, p.status, TC_SITE(3 + t, 8, j));
             if (!__all_sync(0xffffffffu, turn)) {
               ok = false;
               break;
@@ -711,7 +714,7 @@ WATTN_DEVINL void attn_roles(const CUtensorMap &map_q, const CUtensorMap &map_k,
         }
         l += (acc2[0].x + acc2[0].y) + (acc2[1].x + acc2[1].y) + (acc2[2].x + acc2[2].y) +
              (acc2[3].x + acc2[3].y);
-        if (p.pingpong) mbar_arrive(&s.sfu_turn[t ^ 1]);
+        if (p.pingpong) mbar_arrive(&s.sfu_turn[t ^ 1][wq]);
         // P may only overwrite the previous P once the PV reading it is
         // done (also across units), and O may only be rescaled once the
         // previous PV of this unit has added to it.
@@ -885,7 +888,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s.o_free[t], kBM);
       mbar_init(&s.ep_full[0][t], kBM);
       mbar_init(&s.ep_full[1][t], kBM);
-      mbar_init(&s.sfu_turn[t], kBM);
+      for (int q = 0; q < 4; ++q) mbar_init(&s.sfu_turn[t][q], 32);
       mbar_init(&s.part_bar[t][0], kBM);
       mbar_init(&s.part_bar[t][1], kBM);
       mbar_init(&s.merge_bar[t], 1);
@@ -1154,7 +1157,6 @@ int launch_attn_tc(const void *q, const void *k, const void *v, void *o, int in_
     }
     if (ws != nullptr) {
       p.sk_tiles = T;
-      p.pingpong = 0;  // measured slower under the split schedule on B200
       p.by_tiles = FastDiv::make((uint32_t)T);
       p.cnt = reinterpret_cast<int *>(ws);
       p.part = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(ws) + kCounterBytes);
