@@ -590,7 +590,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-extras", action="store_true", help="headline only")
-    ap.add_argument("--only", choices=["all", "enc", "dec", "xdec", "proj", "block"], default="all",
+    ap.add_argument("--only", choices=["all", "enc", "dec", "xdec", "proj", "block", "c1", "c2"],
+                    default="all",
                     help="profiling aid: run one workload only")
     ap.add_argument("--layers", type=int, default=None,
                     help="profiling aid: layers of the workload --only selects (config 3 by default)")
@@ -638,6 +639,9 @@ def main():
         return
     if a.only == "block":
         print(json.dumps({"encoder_block_only": bench_encoder_block(W, a.steps, warmup)}))
+        return
+    if a.only in ("c1", "c2"):
+        print(json.dumps({f"{a.only}_only": bench_small(W, a.only, a.steps, warmup)}))
         return
     enc = bench_encoder(W, rank, world, a.steps, warmup, a.e2e_steps)
     peaks = load_peaks()

@@ -10,9 +10,14 @@
 // the keys in 64-key tiles with the online-softmax recurrence of
 // attention.rs:173-201, in the exp2 domain (q is pre-scaled by
 // scale*log2(e)). Thread (ty, tx) = (tid/8, tid%8) holds a 4 x 8 block of the
-// score tile (rows 4ty.., keys 8tx..) and the same block of the output
-// (rows 4ty.., dims 8tx..); the 8 threads of a row reduce with shuffles.
-// Q and K are kept d-major in shared memory so both products read float4s.
+// score tile (rows 4ty.., keys 4tx..4tx+3 and 32+4tx..32+4tx+3) and the same
+// block of the output (rows 4ty.., the same dims); the 8 threads of a row
+// reduce with shuffles. Q and K are kept d-major in shared memory so both
+// products read float4s. With the two 4-column halves 32 columns apart, the
+// 8 threads of one quarter-warp read 8 consecutive float4s of a K or V row
+// (every bank once); 8 contiguous columns per thread put threads tx and
+// tx+4 on the same banks (a two-way conflict on every such read, measured
+// with ncu as 43 % of the kernel's shared-memory wavefronts).
 //
 // Small problems (few query blocks x heads for the SMs, e.g. Whisper-tiny's
 // one utterance of 6 heads: 144 CTAs) split the keys: each of up to three
@@ -120,8 +125,8 @@ __global__ void __launch_bounds__(kThreads) attn_fwd_f32_kernel(const F32Params 
 #pragma unroll 8
     for (int d = 0; d < 64; ++d) {
       const float4 a = *reinterpret_cast<const float4 *>(&qt[d][4 * ty]);
-      const float4 b0 = *reinterpret_cast<const float4 *>(&kt[d][8 * tx]);
-      const float4 b1 = *reinterpret_cast<const float4 *>(&kt[d][8 * tx + 4]);
+      const float4 b0 = *reinterpret_cast<const float4 *>(&kt[d][4 * tx]);
+      const float4 b1 = *reinterpret_cast<const float4 *>(&kt[d][32 + 4 * tx]);
       const float av[4] = {a.x, a.y, a.z, a.w};
       const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
@@ -138,7 +143,7 @@ __global__ void __launch_bounds__(kThreads) attn_fwd_f32_kernel(const F32Params 
       float mx = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
-        if (8 * tx + c >= lim) s[i][c] = -INFINITY;
+        if ((c < 4 ? 4 * tx + c : 28 + 4 * tx + c) >= lim) s[i][c] = -INFINITY;
         mx = fmaxf(mx, s[i][c]);
       }
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
@@ -160,14 +165,14 @@ __global__ void __launch_bounds__(kThreads) attn_fwd_f32_kernel(const F32Params 
       m[i] = m_new;
 #pragma unroll
       for (int c = 0; c < 8; ++c) acc[i][c] *= alpha;
-      *reinterpret_cast<float4 *>(&ps[4 * ty + i][8 * tx]) =
+      *reinterpret_cast<float4 *>(&ps[4 * ty + i][4 * tx]) =
           make_float4(s[i][0], s[i][1], s[i][2], s[i][3]);
-      *reinterpret_cast<float4 *>(&ps[4 * ty + i][8 * tx + 4]) =
+      *reinterpret_cast<float4 *>(&ps[4 * ty + i][32 + 4 * tx]) =
           make_float4(s[i][4], s[i][5], s[i][6], s[i][7]);
     }
     __syncthreads();
 
-    // O += P V for rows 4ty.., dims 8tx..
+    // O += P V for rows 4ty.., dims 4tx.. and 32+4tx..
 #pragma unroll 4
     for (int kk = 0; kk < kBN; kk += 4) {
       float4 pr[4];
@@ -175,8 +180,8 @@ __global__ void __launch_bounds__(kThreads) attn_fwd_f32_kernel(const F32Params 
       for (int i = 0; i < 4; ++i) pr[i] = *reinterpret_cast<const float4 *>(&ps[4 * ty + i][kk]);
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const float4 v0 = *reinterpret_cast<const float4 *>(&vs[kk + u][8 * tx]);
-        const float4 v1 = *reinterpret_cast<const float4 *>(&vs[kk + u][8 * tx + 4]);
+        const float4 v0 = *reinterpret_cast<const float4 *>(&vs[kk + u][4 * tx]);
+        const float4 v1 = *reinterpret_cast<const float4 *>(&vs[kk + u][32 + 4 * tx]);
         const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -196,9 +201,9 @@ __global__ void __launch_bounds__(kThreads) attn_fwd_f32_kernel(const F32Params 
       if (qrow >= p.t_q) continue;
       float *dst = p.part + ((((int64_t)b * gridDim.y + head) * p.t_q + qrow) * p.n_splits + split) *
                                 kPartFloats;
-      *reinterpret_cast<float4 *>(dst + 8 * tx) =
+      *reinterpret_cast<float4 *>(dst + 4 * tx) =
           make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
-      *reinterpret_cast<float4 *>(dst + 8 * tx + 4) =
+      *reinterpret_cast<float4 *>(dst + 32 + 4 * tx) =
           make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
       if (tx == 0) {
         dst[64] = m[i];
@@ -212,10 +217,10 @@ __global__ void __launch_bounds__(kThreads) attn_fwd_f32_kernel(const F32Params 
     const int qrow = q0 + 4 * ty + i;
     if (qrow >= p.t_q) continue;
     const float inv = l[i] > 0.f ? 1.f / l[i] : 0.f;
-    float *dst = p.o + (int64_t)b * p.o_bs + (int64_t)qrow * p.o_rs + head * kHeadDim + 8 * tx;
+    float *dst = p.o + (int64_t)b * p.o_bs + (int64_t)qrow * p.o_rs + head * kHeadDim + 4 * tx;
     *reinterpret_cast<float4 *>(dst) =
         make_float4(acc[i][0] * inv, acc[i][1] * inv, acc[i][2] * inv, acc[i][3] * inv);
-    *reinterpret_cast<float4 *>(dst + 4) =
+    *reinterpret_cast<float4 *>(dst + 32) =
         make_float4(acc[i][4] * inv, acc[i][5] * inv, acc[i][6] * inv, acc[i][7] * inv);
   }
 }
