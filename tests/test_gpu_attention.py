@@ -338,6 +338,48 @@ def test_f32_key_splits(W, oracle, cfg):
         check_f32(out, ref, f"f32 key splits {cfg}")
 
 
+@pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
+def test_f32_later_key_tile_moves_the_offset(W, oracle, causal):
+    """f32: keys 256..383 share a large component with every query (scores
+    in the exp2 domain jump by about 11 there, past the 2^8 rescale
+    threshold for most rows), so the running offset moves on a later key
+    tile and the partial output in tensor memory is rescaled; 1e-5."""
+    import torch
+    b, t_q, t_kv, h = 1, 300, 700, 2
+    d = h * 64
+    q = randn(801, t_q * d).reshape(t_q, d)
+    k = randn(802, t_kv * d).reshape(t_kv, d)
+    v = randn(803, t_kv * d)
+    q[:, 0::64] += np.float32(3.0)
+    k[256:384, 0::64] += np.float32(20.0)
+    q, k = q.ravel(), k.ravel()
+    off = t_kv - t_q if causal else 0
+    if causal:
+        ref = oracle.mha_with_cache(q, k, v, t_q, t_kv, off, h, d)
+    else:
+        ref = oracle.flash_attention_2_batched(q, k, v, b, t_q, t_kv, h, d, False)
+    out = _run_fwd(W, *(torch.from_numpy(x).cuda() for x in (q, k, v)), 0, b, t_q, t_kv, h,
+                   causal, off)
+    check_f32(out, ref, f"f32 offset move causal={causal}")
+
+
+def test_attention_host_f32_two_streams(W, oracle):
+    """wattn_attention_host with f32 inputs: 7 whisper-tiny utterances in
+    chunks of 3, 3 and 1 on two streams, each stream with its own split
+    operands; 1e-5 on utterances of every chunk."""
+    import torch
+    b, t, h = 7, 1500, 6
+    d = h * 64
+    q, k, v = randn(71, b * t * d), randn(72, b * t * d), randn(73, b * t * d)
+    o = torch.empty(b * t * d, dtype=torch.float32)
+    W.attention_host(*(torch.from_numpy(x) for x in (q, k, v)), o, b, t, t, h, 0.125)
+    out = o.numpy().reshape(b, t * d)
+    for u in (0, 4, 6):
+        sl = slice(u * t * d, (u + 1) * t * d)
+        ref = oracle.flash_attention_2(q[sl], k[sl], v[sl], t, t, h, d, False)
+        check_f32(out[u], ref, f"f32 host utterance {u}")
+
+
 def test_single_token_and_cache_mirrors(W, oracle):
     h, d = 4, 256
     for t_kv in (1, 63, 257, 1500):

@@ -324,7 +324,7 @@ int attention_device(const void *q, const void *k, const void *v, void *o, int i
   if (in_dt == WATTN_F32)
     return launch_attn_f32((const float *)q, (const float *)k, (const float *)v, (float *)o, batch,
                            t_q, t_kv, n_heads, q_rs, kv_rs, o_rs, q_bs, kv_bs, o_bs, scale,
-                           causal, q_pos_offset, st);
+                           causal, q_pos_offset, st, split_ws, split_ws_bytes);
   return launch_attn_tc(q, k, v, o, in_dt, out_dt, batch, t_q, t_kv, n_heads, q_rs, kv_rs, o_rs,
                         q_bs, kv_bs, o_bs, scale, causal, q_pos_offset, st, split_ws,
                         split_ws_bytes);
@@ -444,16 +444,17 @@ int attention_host(const void *q, const void *k, const void *v, void *o, int in_
     if ((rc = grow(&h->buf[i], &h->buf_bytes[i], per * chunk, false, h->st[i])) != WATTN_OK)
       return finish_host(h, rc);
   // Each stream's kernels keep their workspaces (key-tile split partials,
-  // V's f16 copy for bf16 inputs) apart.
-  if (in_dt != WATTN_F32) {
+  // V's f16 copy for bf16 inputs, the split operands of f32 inputs) apart.
+  {
     int dev = 0, n_sm = 0;
     if (cudaGetDevice(&dev) != cudaSuccess ||
         cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
       return finish_host(h, check_launch("attention_host: device query"));
+    const size_t ws_need = in_dt == WATTN_F32
+                               ? attn_f32_workspace_bytes(chunk, t_q, t_kv, n_heads, n_sm)
+                               : attn_workspace_bytes(in_dt, chunk, t_kv, n_heads, n_sm);
     for (int i = 0; i < 2; ++i)
-      if ((rc = grow(&h->ws[i], &h->ws_bytes[i],
-                     attn_workspace_bytes(in_dt, chunk, t_kv, n_heads, n_sm), true,
-                     h->st[i])) != WATTN_OK)
+      if ((rc = grow(&h->ws[i], &h->ws_bytes[i], ws_need, true, h->st[i])) != WATTN_OK)
         return finish_host(h, rc);
   }
   for (int c0 = 0, ci = 0; c0 < batch; c0 += chunk, ++ci) {

@@ -97,11 +97,17 @@ size_t attn_split_workspace_bytes(int n_sm);
 // Whole workspace of one launch_attn_tc call on a device of n_sm SMs.
 size_t attn_workspace_bytes(int in_dtype, int batch, int t_kv, int n_heads, int n_sm);
 
-// f32 CUDA-core attention (attn_f32.cu).
+// f32 attention on the tensor cores, 3xTF32 (attn_f32.cu). Its workspace
+// (ws: a caller's 256-byte aligned buffer of ws_bytes, which must then have
+// attn_f32_workspace_bytes() bytes, or, with ws NULL, the calling thread's)
+// holds the split K and V^T operands, the key-split partials and counters.
 int launch_attn_f32(const float *q, const float *k, const float *v, float *o, int batch,
                     int t_q, int t_kv, int n_heads, int64_t q_rs, int64_t kv_rs, int64_t o_rs,
                     int64_t q_bs, int64_t kv_bs, int64_t o_bs, float scale, int causal,
-                    int q_pos_offset, cudaStream_t stream);
+                    int q_pos_offset, cudaStream_t stream, void *ws = nullptr,
+                    size_t ws_bytes = 0);
+// Workspace of one launch_attn_f32 call on a device of n_sm SMs (causal or not).
+size_t attn_f32_workspace_bytes(int batch, int t_q, int t_kv, int n_heads, int n_sm);
 
 // y[m][n] = x[m][k] W[n][k]^T (+ bias[n]) on the tensor cores (linear_tc.cu);
 // x and W 16-bit of the same type, 16-byte aligned, row strides whose byte
