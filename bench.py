@@ -4,8 +4,10 @@
 
 Headline (``value``): config 3, the Whisper-large-v3 encoder self-attention
 stack -- 32 utterances x 20 heads x T=1500 x head dim 64, bf16 Q/K/V drawn
-N(0,1) with a fresh seed per layer, 32 layers, sharded by utterance across
-the N ranks (strong scaling of the fixed 32-utterance batch). One step is the
+N(0,1) with a fresh seed per layer, 32 layers. Utterances are independent
+(no collective on the data path): by default every rank runs its own
+32-utterance batch (weak scaling, global batch 32 x N); ``--scaling strong``
+shares one 32-utterance batch out over the ranks instead. One step is the
 32-layer stack; each layer's inputs (368.6 MB) exceed the 126 MB L2, so no
 flush is needed between launches. ``value`` = algorithmic FLOPs of all ranks
 (4 * B * H * T^2 * D per layer) / the max over ranks of the device time.
@@ -44,8 +46,15 @@ C4 = dict(utterances=32, beams=5, heads=20, layers=32, t_audio=1500)
 METRIC = "enc attn TFLOP/s & dec attn KV GB/s per B200, % roofline, at 1/2/4/8 GPUs"
 
 
+SCALING = "weak"  # or "strong" (--scaling)
+
+
 def shard(n_items: int, rank: int, world: int) -> tuple[int, int]:
-    """Contiguous [lo, hi) share of n_items for `rank` (sizes differ by <= 1)."""
+    """[lo, hi) of the global item range that `rank` processes: under weak
+    scaling every rank has n_items of its own (rank * n_items ..); under
+    strong scaling a contiguous share of n_items (sizes differ by <= 1)."""
+    if SCALING == "weak":
+        return rank * n_items, (rank + 1) * n_items
     base, extra = divmod(n_items, world)
     lo = rank * base + min(rank, extra)
     return lo, lo + base + (1 if rank < extra else 0)
@@ -596,7 +605,12 @@ def main():
     ap.add_argument("--layers", type=int, default=None,
                     help="profiling aid: layers of the workload --only selects (config 3 by default)")
     ap.add_argument("--batch", type=int, default=None, help="profiling aid: config 3 batch")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak",
+                    help="weak: each rank runs the whole per-GPU workload; strong: the ranks "
+                         "share one workload")
     a = ap.parse_args()
+    global SCALING
+    SCALING = a.scaling
     if a.layers:
         {"dec": C5, "xdec": C4}.get(a.only, C3)["layers"] = a.layers
     if a.batch:
@@ -614,7 +628,7 @@ def main():
         print(json.dumps({
             "impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "TFLOP/s",
             "n_gpus": a.gpus, "steps": a.steps, "warmup": warmup, "ms_per_step": step_ms,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": SCALING, "vs_baseline": None, "dtype": "f32",
             "data": "synthetic",
             "config": {"workload": "c3_large_v3_encoder_self_attention", "global_batch": C3["batch"],
                        "heads": C3["heads"], "seq_len": C3["t"], "layers": C3["layers"],
@@ -665,9 +679,11 @@ def main():
     line = {
         "metric": METRIC, "value": enc["value"], "unit": "TFLOP/s", "n_gpus": world,
         "steps": a.steps, "warmup": warmup, "ms_per_step": enc["ms"] / a.steps,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded N(0,1) Q/K/V, fresh seed per layer)",
-        "config": {"workload": "c3_large_v3_encoder_self_attention", "global_batch": C3["batch"],
+        "higher_is_better": True, "scaling": SCALING, "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) Q/K/V, fresh seed per layer and rank)",
+        "config": {"workload": "c3_large_v3_encoder_self_attention",
+                   "global_batch": C3["batch"] * world if SCALING == "weak" else C3["batch"],
+                   "per_gpu_batch": enc["local_batch"],
                    "heads": C3["heads"], "head_dim": 64, "seq_len": C3["t"], "layers": C3["layers"],
                    "parallelism": f"utterance shards x{world} (no collective)",
                    "l2": "inputs exceed L2 (368.6 MB per layer); no flush needed"},

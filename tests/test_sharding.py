@@ -1,5 +1,6 @@
 """Multi-rank host logic on CPU (gloo, world size 2): the utterance shards of
-bench.py cover every utterance exactly once with no exchange between ranks,
+bench.py (strong scaling: one batch shared out; weak scaling: a batch per
+rank) cover every utterance exactly once with no exchange between ranks,
 each rank's shard reproduces the single-process result of the oracle on its
 utterances, and the timing reductions give the max (time) and the sum (work)
 over ranks."""
@@ -13,8 +14,9 @@ import torch.multiprocessing as mp
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-def test_shards_partition_every_config():
+def test_shards_partition_every_config(monkeypatch):
     import bench
+    monkeypatch.setattr(bench, "SCALING", "strong")
     for n in (1, 5, 32, 64, 160, 320):
         for world in (1, 2, 3, 4, 8):
             got = []
@@ -25,6 +27,19 @@ def test_shards_partition_every_config():
             assert got == list(range(n))
             sizes = [bench.shard(n, r, world)[1] - bench.shard(n, r, world)[0] for r in range(world)]
             assert max(sizes) - min(sizes) <= 1
+
+
+def test_weak_scaling_gives_each_rank_a_whole_batch(monkeypatch):
+    import bench
+    monkeypatch.setattr(bench, "SCALING", "weak")
+    for n in (1, 5, 32, 64, 320):
+        for world in (1, 2, 4, 8):
+            got = []
+            for r in range(world):
+                lo, hi = bench.shard(n, r, world)
+                assert hi - lo == n
+                got.extend(range(lo, hi))
+            assert got == list(range(n * world))
 
 
 def _free_port():
@@ -43,7 +58,8 @@ def _worker(rank, world, port, out_dir):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     import bench
     from oracle import oracle as O
-    # A small encoder batch sharded like config 3.
+    bench.SCALING = "strong"
+    # A small encoder batch sharded like config 3 under strong scaling.
     batch, t, h = 5, 40, 2
     d = h * 64
     rng = np.random.default_rng(0)
