@@ -78,8 +78,10 @@ int wattn_device_status(int device, int *status);
  * decoder.rs:864's). Rows whose every key is masked, and t_kv == 0, give 0.
  *
  * in_dtype  WATTN_F16 / WATTN_BF16: tcgen05 tensor-core kernel, f32
- *           accumulation. WATTN_F32: f32 CUDA-core kernel (the reference's
- *           own precision).
+ *           accumulation. WATTN_F32: tcgen05 kernel on split-f16 operands
+ *           (each f32 value as a hi and a lo f16 part, three products per
+ *           product), f32 softmax and accumulation: the reference's
+ *           precision (1e-5).
  * out_dtype WATTN_F32, or the input type.
  * Strides are in elements: *_row_stride between rows t and t+1 of one
  * utterance, *_batch_stride between utterances. K and V share strides.

@@ -1,9 +1,9 @@
 """Encoder / general attention on the GPU against the CPU oracle.
 
 f16/bf16 inputs (tcgen05 kernel): max-abs <= 2e-3 and cosine > 0.9999 against
-the oracle run on the same rounded inputs. f32 inputs (CUDA-core kernel and
-the reference-signature host mirrors): max-abs <= 1e-5, the reference's own
-bar, against the reference tests' golden vectors.
+the oracle run on the same rounded inputs. f32 inputs (split-f16 products on
+the tensor cores, and the reference-signature host mirrors): max-abs <= 1e-5,
+the reference's own bar, against the reference tests' golden vectors.
 """
 import os
 
