@@ -323,6 +323,54 @@ def test_f32_tiny_encoder_shape(W, oracle):
     check_f32(host, ref, "C1 host mirror")
 
 
+@pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
+def test_f32_magnitudes_far_from_one(W, oracle, causal):
+    """f32 operands are carried in f16 parts under power-of-two scales chosen
+    per 128-key tile (K, V) and per 128-row query block (Q). Here Q is near
+    1e-3, K near 3e3, and V's key tiles alternate between ~1e4 and ~1e-4:
+    every scale differs from the next, and the small V tiles must still
+    count. Bar: 1e-5 of V's largest magnitude (the reference's 1e-5 is for
+    values of order one)."""
+    import torch
+    b, t_q, t_kv, h = 1, 260, 700, 2
+    d = h * 64
+    q = randn(901, t_q * d) * np.float32(1e-3)
+    k = randn(902, t_kv * d) * np.float32(3e3)
+    v = randn(903, t_kv * d).reshape(t_kv, d)
+    for t0 in range(0, t_kv, 128):
+        v[t0:t0 + 128] *= np.float32(1e4 if (t0 // 128) % 2 == 0 else 1e-4)
+    v = v.ravel()
+    off = t_kv - t_q if causal else 0
+    if causal:
+        ref = oracle.mha_with_cache(q, k, v, t_q, t_kv, off, h, d)
+    else:
+        ref = oracle.flash_attention_2_batched(q, k, v, b, t_q, t_kv, h, d, False)
+    out = _run_fwd(W, *(torch.from_numpy(x).cuda() for x in (q, k, v)), 0, b, t_q, t_kv, h,
+                   causal, off)
+    check_f32(out, ref, f"f32 magnitudes causal={causal}", tol=1e-5 * float(np.abs(v).max()))
+
+
+def test_f32_fused_qkv_and_padded_output(W, oracle):
+    """f32 Q, K, V read in place from the encoder's fused [T, 3 d] rows, and
+    an output with padded rows (row stride d + 64): the padding is left as
+    it was."""
+    import torch
+    t, h = 700, 6
+    d = h * 64
+    qkv = randn(41, t * 3 * d).reshape(t, 3 * d)
+    ref = oracle.flash_attention_2(np.ascontiguousarray(qkv[:, :d]),
+                                   np.ascontiguousarray(qkv[:, d:2 * d]),
+                                   np.ascontiguousarray(qkv[:, 2 * d:]), t, t, h, d, False)
+    qkv_d = torch.from_numpy(qkv.ravel()).cuda()
+    o = torch.full((t, d + 64), 7.0, dtype=torch.float32, device="cuda")
+    W.attention_fwd(qkv_d, qkv_d[d:], qkv_d[2 * d:], o, batch=1, t_q=t, t_kv=t, n_heads=h,
+                    scale=0.125, q_row_stride=3 * d, kv_row_stride=3 * d, o_row_stride=d + 64)
+    torch.cuda.synchronize()
+    out = o.cpu().numpy()
+    check_f32(out[:, :d], ref.reshape(t, d), "f32 fused qkv")
+    assert bool((out[:, d:] == 7.0).all())
+
+
 @pytest.mark.parametrize("cfg", [(1, 100, 1000, 2), (2, 70, 777, 3), (1, 64, 256, 1)],
                          ids=lambda c: "b{}_tq{}_tkv{}_h{}".format(*c))
 def test_f32_key_splits(W, oracle, cfg):
