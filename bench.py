@@ -593,7 +593,7 @@ def cpu_baseline(seconds: float = 10.0):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=40)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["wattn", "reference"], default="wattn")
     ap.add_argument("--e2e-steps", type=int, default=3)
