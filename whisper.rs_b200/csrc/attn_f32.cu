@@ -355,6 +355,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tmem_alloc(&s.tmem_base, kTcTmemCols);
     tmem_relinquish();
   }
+  // The softmax threads' Q half-rows are read before the dependency wait:
+  // the pre-pass does not write Q, and every kernel ahead of it in the
+  // stream has completed when this grid's CTAs start (the pre-pass waits
+  // for them before it lets this grid launch), so the load's latency hides
+  // behind the set-up and the wait.
+  const int quarter = warp & 3, half = (warp >> 2) & 1;
+  const int row = quarter * 32 + lane, qrow = q0 + row;
+  float4 x[8];
+  if (warp < kTcTmaWarp) {
+    const float *src = p.q + (int64_t)b * p.q_bs + (int64_t)qrow * p.q_rs + head * kHeadDim +
+                       32 * half;
+    const bool q_in = qrow < p.t_q;
+#pragma unroll
+    for (int e4 = 0; e4 < 8; ++e4)
+      x[e4] = q_in ? __ldg(reinterpret_cast<const float4 *>(src + 4 * e4))
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -364,8 +381,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   volatile int *abort = &s.abort;
   // The softmax threads' results (row m and l, the half's 32 output
   // columns), read by the split merge below.
-  const int quarter = warp & 3, half = (warp >> 2) & 1;
-  const int row = quarter * 32 + lane, qrow = q0 + row;
   float m = -INFINITY, l = 0.f;
   int ev_min = 100;  // O is accumulated at the scale 2^ev_min (below)
   bool have = false;
@@ -490,18 +505,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // Range exponents from the pre-pass: e_q of this query block (every CTA
     // of a cluster has the same rows) and the key tiles'. V's tiles come
     // with their own exponents e_v(t); P is weighted by 2^(ev_min - e_v(t))
-    // so that one accumulator holds every tile at the scale 2^ev_min. The
-    // Q rows, e_q and the V exponents are loaded together.
+    // so that one accumulator holds every tile at the scale 2^ev_min.
     const int *ek_row = p.ek + (int64_t)bh * p.n_kv_tiles + kv_beg / kTcKeys;
     const int *ev_row = p.ev + (int64_t)bh * p.n_kv_tiles + kv_beg / kTcKeys;
-    const float *src = p.q + (int64_t)b * p.q_bs + (int64_t)qrow * p.q_rs + head * kHeadDim +
-                       32 * half;
-    const bool q_in = qrow < p.t_q;
-    float4 x[8];
-#pragma unroll
-    for (int e4 = 0; e4 < 8; ++e4)
-      x[e4] = q_in ? __ldg(reinterpret_cast<const float4 *>(src + 4 * e4))
-                   : make_float4(0.f, 0.f, 0.f, 0.f);
     const int e_q = __ldg(p.eq + (int64_t)bh * p.n_qblk + qblk);
     for (int i = lane; i < n_tiles; i += 32) ev_min = min(ev_min, __ldg(ev_row + i));
 #pragma unroll
