@@ -705,23 +705,32 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int q = 0; q < 4; ++q) owned += (q * S / 4 == split) ? 32u : 0u;
       mbar_arrive_expect_tx(&s.land, (uint32_t)(S - 1) * owned * kRowBytes);
     }
+    // This CTA's own ring is free once its last products are done (have:
+    // every softmax thread saw them), so its outgoing rows are staged before
+    // the cluster barrier, which also orders the staging for the copies.
+    if (warp < kTcTmaWarp && owner != split && have) {
+      float *mine = reinterpret_cast<float *>(ring + split * kPartBytes) + row * kPartFloats;
+      const float sc = pow2(-ev_min);
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<float4 *>(mine + 32 * half + 4 * c) =
+            make_float4(__uint_as_float(o[4 * c]) * sc, __uint_as_float(o[4 * c + 1]) * sc,
+                        __uint_as_float(o[4 * c + 2]) * sc, __uint_as_float(o[4 * c + 3]) * sc);
+      if (half == 0) *reinterpret_cast<float4 *>(mine + 64) = make_float4(m, l, 0.f, 0.f);
+      fence_proxy_async_smem();
+    }
     __syncwarp();
     cluster_sync_all();
     bool landed = true;
     if (warp < kTcTmaWarp) {
-      float *slot = reinterpret_cast<float *>(ring + split * kPartBytes);
       if (owner != split) {
-        float *mine = slot + row * kPartFloats;
-        const float sc = pow2(-ev_min);
-#pragma unroll
-        for (int c = 0; c < 8; ++c)
-          *reinterpret_cast<float4 *>(mine + 32 * half + 4 * c) =
-              make_float4(__uint_as_float(o[4 * c]) * sc, __uint_as_float(o[4 * c + 1]) * sc,
-                          __uint_as_float(o[4 * c + 2]) * sc, __uint_as_float(o[4 * c + 3]) * sc);
-        if (half == 0)
-          *reinterpret_cast<float4 *>(mine + 64) = make_float4(m, have ? l : 0.f, 0.f, 0.f);
-        fence_proxy_async_smem();
-        pair_sync_and(true, quarter);
+        if (!have && half == 0) {
+          // no result (a wait gave up): the rows go out marked empty, l = 0
+          float *mine = reinterpret_cast<float *>(ring + split * kPartBytes) + row * kPartFloats;
+          *reinterpret_cast<float4 *>(mine + 64) = make_float4(m, 0.f, 0.f, 0.f);
+          fence_proxy_async_smem();
+        }
+        if (!have) pair_sync_and(true, quarter);
         if (half == 0 && lane == 0) {
           const uint32_t off = split * kPartBytes + quarter * 32 * kRowBytes;
           bulk_copy_to_cluster(cluster_map(smem_u32(ring + off), owner), ring + off,
