@@ -253,7 +253,7 @@ def bench_encoder(W, rank, world, steps, warmup, e2e_steps):
     # ---- e2e: host buffers (pinned), copies inside the timed region
     e2e = None
     if e2e_steps > 0:
-        n_host = min(L, 4)  # distinct host layers cycled (each > L2)
+        n_host = min(L, 2)  # distinct host layers cycled (each > L2; pinned memory per rank ~1 GB)
         host = []
         for i in range(n_host):
             q, k, v, _ = layers[i]
