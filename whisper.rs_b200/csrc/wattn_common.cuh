@@ -312,37 +312,6 @@ WATTN_DEVINL void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uin
       : "memory");
 }
 
-// D[tmem] (+)= A[smem] * B[smem]^T, kind::tf32 (32-bit operands of which the
-// tensor core reads the tf32 part, f32 accumulation).
-WATTN_DEVINL void umma_ss_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                               uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// D[tmem] (+)= A[tmem] * B[smem], kind::tf32.
-WATTN_DEVINL void umma_ts_tf32(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                               uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// x rounded to tf32 (10 explicit mantissa bits, to nearest, ties away from
-// zero), returned as an f32 whose low 13 bits are zero.
-WATTN_DEVINL float round_tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
-}
-
 // Arrives once on `bar` when every tcgen05 operation issued so far by this
 // thread has completed.
 WATTN_DEVINL void umma_commit(uint64_t *bar) {
@@ -420,12 +389,6 @@ WATTN_DEVINL uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32
   d |= (uint64_t)1 << 46;
   d |= (uint64_t)2 << 61;
   return d;
-}
-
-// Instruction descriptor of kind::tf32 with f32 accumulation (A and B
-// K-major; A and B format 2 = tf32).
-__host__ __device__ constexpr uint32_t idesc_tf32(uint32_t m, uint32_t n) {
-  return (1u << 4) | (2u << 7) | (2u << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
 }
 
 // Instruction descriptor of kind::f16 with f32 accumulation.
