@@ -350,6 +350,31 @@ def test_f32_magnitudes_far_from_one(W, oracle, causal):
     check_f32(out, ref, f"f32 magnitudes causal={causal}", tol=1e-5 * float(np.abs(v).max()))
 
 
+def test_f32_batch_strides_with_gaps(W, oracle):
+    """f32, 3 utterances whose Q, K/V and O sit with gaps between them
+    (batch strides above t * row stride) and 129 / 300 rows (a ragged
+    query block and key tile): the pre-pass and the output's tensor map
+    follow the strides; the gaps are left as they were."""
+    import torch
+    b, t_q, t_kv, h = 3, 129, 300, 2
+    d = h * 64
+    q_bs, kv_bs, o_bs = (t_q + 5) * d, (t_kv + 3) * d, (t_q + 7) * d
+    q = randn(961, b * q_bs).reshape(b, q_bs)
+    k = randn(962, b * kv_bs).reshape(b, kv_bs)
+    v = randn(963, b * kv_bs).reshape(b, kv_bs)
+    o = torch.full((b * o_bs,), 5.0, dtype=torch.float32, device="cuda")
+    W.attention_fwd(*(torch.from_numpy(x.ravel()).cuda() for x in (q, k, v)), o, batch=b,
+                    t_q=t_q, t_kv=t_kv, n_heads=h, scale=0.125, q_batch_stride=q_bs,
+                    kv_batch_stride=kv_bs, o_batch_stride=o_bs)
+    torch.cuda.synchronize()
+    out = o.cpu().numpy().reshape(b, o_bs)
+    for u in range(b):
+        ref = oracle.flash_attention_2(q[u, :t_q * d], k[u, :t_kv * d], v[u, :t_kv * d], t_q,
+                                       t_kv, h, d, False)
+        check_f32(out[u, :t_q * d], ref, f"f32 strided utterance {u}")
+        assert bool((out[u, t_q * d:] == 5.0).all())
+
+
 def test_f32_fused_qkv_and_padded_output(W, oracle):
     """f32 Q, K, V read in place from the encoder's fused [T, 3 d] rows, and
     an output with padded rows (row stride d + 64): the padding is left as
