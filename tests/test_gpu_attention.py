@@ -350,6 +350,27 @@ def test_f32_magnitudes_far_from_one(W, oracle, causal):
     check_f32(out, ref, f"f32 magnitudes causal={causal}", tol=1e-5 * float(np.abs(v).max()))
 
 
+@pytest.mark.parametrize("case", ["far_outside_f16", "zero_k", "zero_v"])
+def test_f32_extreme_ranges(W, oracle, case):
+    """f32 values no f16 can hold (Q near 1e20, K near 1e-20, V near 1e30:
+    the range powers of two run to their clamps' neighbourhood), all-zero K
+    (uniform weights) and all-zero V (zero output). Bar: 1e-5 of V's
+    largest magnitude, at least 1e-5."""
+    import torch
+    t_q, t_kv, h = 200, 333, 2
+    d = h * 64
+    q, k, v = randn(971, t_q * d), randn(972, t_kv * d), randn(973, t_kv * d)
+    if case == "far_outside_f16":
+        q, k, v = q * np.float32(1e20), k * np.float32(1e-20), v * np.float32(1e30)
+    elif case == "zero_k":
+        k = np.zeros_like(k)
+    else:
+        v = np.zeros_like(v)
+    ref = oracle.flash_attention_2(q, k, v, t_q, t_kv, h, d, False)
+    out = _run_fwd(W, *(torch.from_numpy(x).cuda() for x in (q, k, v)), 0, 1, t_q, t_kv, h)
+    check_f32(out, ref, f"f32 {case}", tol=max(1e-5, 1e-5 * float(np.abs(v).max())))
+
+
 def test_f32_batch_strides_with_gaps(W, oracle):
     """f32, 3 utterances whose Q, K/V and O sit with gaps between them
     (batch strides above t * row stride) and 129 / 300 rows (a ragged
