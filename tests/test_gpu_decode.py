@@ -61,6 +61,23 @@ def test_decode_many_splits(W, oracle, kv_dt, t_kv):
     check_16bit(out, ref, f"dt={kv_dt} t_kv={t_kv}")
 
 
+@pytest.mark.parametrize("seed", [0, 1, 2, 3])
+@pytest.mark.parametrize("t_kv", [2, 4, 5, 18, 33])
+def test_decode_bf16_short_key_ranges(W, oracle, t_kv, seed):
+    # bf16 q and K/V on the streaming tensor-core kernel with few keys, where
+    # one or two weights dominate each row: P rounded to bf16 alone (8
+    # significant bits) gave max-abs errors up to 5.2e-3 here; the kernel
+    # carries P's rounding residual as a second bf16 part.
+    n_groups, g, h = 11, 14, 20
+    d = h * 64
+    (kd, kf), (vd, vf) = rounded(randn(500 + 7 * seed + t_kv, n_groups * t_kv * d), 2), \
+        rounded(randn(600 + 7 * seed + t_kv, n_groups * t_kv * d), 2)
+    qd, qf = rounded(randn(700 + seed, n_groups * g * d), 2)
+    ref = oracle.decode_grouped(qf, kf, vf, n_groups, g, t_kv, h, d)
+    check_16bit(_decode(W, qd, kd, vd, 0, n_groups, g, t_kv, h), ref, f"bf16 t_kv={t_kv}")
+    check_16bit(_decode(W, qd, kd, vd, 2, n_groups, g, t_kv, h), ref, f"bf16 out t_kv={t_kv}", 2)
+
+
 def test_decode_cross_attention_large_v3(W, oracle):
     # Config 4 at full size, one layer: 32 utterances x 5 beams, 20 heads,
     # f16 K/V of 1500 encoder states shared by the beams of an utterance.

@@ -616,10 +616,9 @@ __device__ void decode_stream_body(const CUtensorMap &map_k, const CUtensorMap &
         const float alpha = ex2(m_r - mc);
         l_r *= alpha;
 #pragma unroll
-        for (int db = 0; db < 8; ++db) {
-          acc[db][0] *= alpha;
-          acc[db][1] *= alpha;
-        }
+        for (int db = 0; db < 8; ++db)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[db][e] *= alpha;
         m_r = mc;
       }
       const float mu = (m_r == -INFINITY) ? 0.f : m_r;
@@ -628,14 +627,22 @@ __device__ void decode_stream_body(const CUtensorMap &map_k, const CUtensorMap &
       for (int nb = 0; nb < 2; ++nb)
 #pragma unroll
         for (int e = 0; e < 2; ++e) pe[nb][e] = ex2(fmaf(sc[nb][e], c, -mu));
+      // P enters the product as two 16-bit parts: rows 0-7 of the A tile
+      // hold the weights rounded to T, rows 8-15 (no query rows there) the
+      // rounding residual p - round(p), also in T. Output rows 8-15 then
+      // gather the residual's products, added to rows 0-7 at the item's end:
+      // P keeps ~16 significant bits with bf16 (the reference's weights
+      // are f32, attention.rs:246-434; bf16's 8 alone gave 2.5e-3 max-abs
+      // errors on short key ranges) at no extra tensor-core instruction.
       uint32_t pa[4];
       pa[0] = pack2<T>(pe[0][0], pe[0][1]);
       pa[2] = pack2<T>(pe[1][0], pe[1][1]);
-      pa[1] = pa[3] = 0u;
-      // Normalise by the rounded weights the tensor core uses.
       {
         const float2 r0 = unpack2<T>(pa[0]), r2 = unpack2<T>(pa[2]);
-        l_r += (r0.x + r0.y) + (r2.x + r2.y);
+        pa[1] = pack2<T>(pe[0][0] - r0.x, pe[0][1] - r0.y);
+        pa[3] = pack2<T>(pe[1][0] - r2.x, pe[1][1] - r2.y);
+        // the f32 weights, which the two parts carry to ~2^-16
+        l_r += (pe[0][0] + pe[0][1]) + (pe[1][0] + pe[1][1]);
       }
       mbar_wait(&s.vfull[stage], ph, abort, p.status, (2 << 24) | (2 << 16) | ((pos & 0xff) << 8));
       {
@@ -654,7 +661,12 @@ __device__ void decode_stream_body(const CUtensorMap &map_k, const CUtensorMap &
     }
     l_r += __shfl_xor_sync(0xffffffffu, l_r, 1);
     l_r += __shfl_xor_sync(0xffffffffu, l_r, 2);
-
+    // the residual's products (output rows 8-15) join the rounded weights'
+#pragma unroll
+    for (int db = 0; db < 8; ++db) {
+      acc[db][0] += acc[db][2];
+      acc[db][1] += acc[db][3];
+    }
 
     // ---- merge the four compute warps (log-sum-exp) into red / s.m / s.l
     compute_sync();  // the previous item's epilogue is done with red, m, l
