@@ -115,6 +115,9 @@ int wattn_attention_fwd(const void *q, const void *k, const void *v, void *o,
  * left zeroed by every call) holds the partials; pass NULL to use a
  * library-owned per-device workspace.
  * q_dtype / out_dtype: F32, F16 or BF16. kv_dtype: F32, F16 or BF16.
+ * k and v: 16-byte aligned, row and group strides multiples of 16 bytes;
+ * q and o: aligned to their element size (a 16-bit q: 4 bytes, with an even
+ * row stride). Misaligned pointers return WATTN_ERR_INVALID.
  * ====================================================================== */
 size_t wattn_decode_workspace_bytes(int n_groups, int group_size, int t_kv,
                                     int n_heads);
@@ -159,7 +162,7 @@ int wattn_decode_fwd_capture(const void *q, const void *k, const void *v, void *
  * f16 or bf16; f32 accumulation). x [m][k] (row stride x_row_stride), W
  * [n][k] (w_row_stride), y [m][n] (y_row_stride) in out_dtype; bias: device
  * f32 [n] or NULL. x and W must be 16-byte aligned with row strides whose
- * byte size is a multiple of 16. */
+ * byte size is a multiple of 16; y and bias aligned to their element size. */
 int wattn_linear_fwd(const void *x, const void *w, const float *bias, void *y,
                      int in_dtype, int out_dtype, int m, int n, int k,
                      int64_t x_row_stride, int64_t w_row_stride,
@@ -292,7 +295,8 @@ int wattn_kv_advance(wattn_kv_cache *cache, const int *slots,
 /* Append n_tokens[i] new K/V rows for slots[i] into `layer`
  * (decoder.rs:631-635). Rows are packed sequence-major as in the reference
  * (k_rows + (sum_{i'<i} n_tokens[i'] + t) * row_stride), width
- * n_heads*64, type src_dtype. slots / n_tokens are host arrays. */
+ * n_heads*64, type src_dtype, aligned to its element size. slots /
+ * n_tokens are host arrays. */
 int wattn_kv_append(wattn_kv_cache *cache, int layer, const int *slots,
                     const int *n_tokens, int n_seqs, const void *k_rows,
                     const void *v_rows, int src_dtype, int64_t row_stride,
@@ -300,7 +304,8 @@ int wattn_kv_append(wattn_kv_cache *cache, int layer, const int *slots,
 
 /* Causal self-attention of the appended rows over each slot's history in
  * `layer` (multi_head_attention_with_cache, decoder.rs:835-892). q / o rows
- * packed like k_rows above. `workspace` as for wattn_decode_fwd
+ * packed like k_rows above, each aligned to its element size (a 16-bit q:
+ * 4 bytes, with an even row stride). `workspace` as for wattn_decode_fwd
  * (wattn_kv_workspace_bytes), or NULL. */
 size_t wattn_kv_workspace_bytes(const wattn_kv_cache *cache, int n_rows);
 int wattn_kv_attend(wattn_kv_cache *cache, int layer, const int *slots,

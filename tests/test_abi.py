@@ -110,3 +110,53 @@ def test_capture_selection_is_validated_first(wattn):
     assert e.value.status in (-1, -2)
     assert (out == 0).all()
 
+
+
+def test_misaligned_pointers_are_argument_errors(wattn):
+    # Kernels that read or write elements one at a time need pointers aligned
+    # to the element size; a caller's misaligned pointer must come back as
+    # WATTN_ERR_INVALID from the host-side checks, never reach a launch.
+    # The addresses below are made up and never dereferenced; on a machine
+    # with a GPU this test stands aside (a check that let one through would
+    # hand the address to a kernel there).
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("made-up device addresses are only passed where no GPU can run them")
+    L = wattn.lib
+    buf = ctypes.create_string_buffer(256)
+    base = 1 << 20  # 16-byte aligned
+    F32, F16 = wattn.F32, wattn.F16
+
+    def last():
+        L.wattn_last_error(buf, 256)
+        return buf.value
+
+    # decode: f32 q, then the f32 output, one byte off
+    rc = L.wattn_decode_fwd(base + 1, base, base, base, F32, F16, F32, 1, 1, 10, 2, 64, 128, 128,
+                            1280, 128, 0.125, None, 0, None)
+    assert rc == -1 and b"aligned" in last()
+    rc = L.wattn_decode_fwd(base, base, base, base + 2, F16, F16, F32, 1, 1, 10, 2, 64, 128, 128,
+                            1280, 128, 0.125, None, 0, None)
+    assert rc == -1 and b"aligned" in last()
+    rc = L.wattn_decode_fwd_noalloc(base, base, base, base + 1, F16, F16, F16, 1, 1, 10, 2, 64,
+                                    128, 128, 1280, 128, 0.125, None)
+    assert rc == -1 and b"aligned" in last()
+    # linear: the output, then the bias
+    rc = L.wattn_linear_fwd(base, base, None, base + 2, F16, F32, 4, 8, 64, 64, 64, 8, None)
+    assert rc == -1 and b"aligned" in last()
+    rc = L.wattn_linear_fwd(base, base, ctypes.cast(base + 2, wattn._fp), base, F16, F32, 4, 8, 64,
+                            64, 64, 8, None)
+    assert rc == -1 and b"aligned" in last()
+    # cross K/V projection: the value bias
+    rc = L.wattn_cross_kv_project(base, base, base, ctypes.cast(base + 1, wattn._fp), base, base,
+                                  F16, F16, 4, 64, 64, 64, None)
+    assert rc == -1 and b"aligned" in last()
+    # encoder block with the residual: the f32 residual stream
+    ws = base << 4
+    rc = L.wattn_encoder_attention_residual(ctypes.cast(base + 2, wattn._fp),
+                                            ctypes.cast(base, wattn._fp),
+                                            ctypes.cast(base, wattn._fp), base,
+                                            ctypes.cast(base, wattn._fp), base,
+                                            ctypes.cast(base, wattn._fp), F16, 1, 4, 1, ws,
+                                            1 << 30, None)
+    assert rc == -1 and b"aligned" in last()

@@ -350,6 +350,8 @@ int validate_decode(const void *q, const void *k, const void *v, const void *o, 
   if (kv_gs < 0) return set_error(WATTN_ERR_INVALID, "negative group stride");
   if (n_groups == 0) return WATTN_OK;
   if (!q || !o || (t_kv > 0 && (!k || !v))) return set_error(WATTN_ERR_INVALID, "NULL tensor");
+  if (!elem_aligned(q, q_dt) || !elem_aligned(o, out_dt))
+    return set_error(WATTN_ERR_INVALID, "q and o must be aligned to their element size");
   const int es = elem_size(kv_dt);
   if (!aligned16(k) || !aligned16(v) || (kv_rs * es) % 16 || (kv_gs * es) % 16)
     return set_error(WATTN_ERR_INVALID,
@@ -817,7 +819,8 @@ int wattn_capture_cross_attention_heads(const float *q, const float *k, size_t n
 }
 
 int validate_linear(const void *x, const void *w, const void *y, int in_dtype, int out_dtype,
-                    int m, int n, int k, int64_t x_rs, int64_t w_rs, int64_t y_rs) {
+                    int m, int n, int k, int64_t x_rs, int64_t w_rs, int64_t y_rs,
+                    const float *bias) {
   if (in_dtype != WATTN_F16 && in_dtype != WATTN_BF16)
     return set_error(WATTN_ERR_UNSUPPORTED, "linear: inputs must be f16 or bf16");
   if (!valid_dtype(out_dtype)) return set_error(WATTN_ERR_INVALID, "linear: bad output dtype");
@@ -830,6 +833,8 @@ int validate_linear(const void *x, const void *w, const void *y, int in_dtype, i
       ((x_rs * 2) & 15) || ((w_rs * 2) & 15))
     return set_error(WATTN_ERR_INVALID,
                      "linear: x and W need 16-byte aligned rows (base and row stride)");
+  if (!elem_aligned(y, out_dtype) || !elem_aligned(bias, WATTN_F32))
+    return set_error(WATTN_ERR_INVALID, "linear: y and the bias must be aligned to their element size");
   return WATTN_OK;
 }
 
@@ -838,7 +843,7 @@ int wattn_linear_fwd(const void *x, const void *w, const float *bias, void *y, i
                      int64_t w_row_stride, int64_t y_row_stride, void *stream) {
   clear_error();
   int rc = validate_linear(x, w, y, in_dtype, out_dtype, m, n, k, x_row_stride, w_row_stride,
-                           y_row_stride);
+                           y_row_stride, bias);
   if (rc != WATTN_OK || m == 0 || n == 0) return rc;
   return launch_linear(x, w, bias, y, in_dtype, out_dtype, m, n, k, x_row_stride, w_row_stride,
                        y_row_stride, (cudaStream_t)stream);
@@ -850,10 +855,10 @@ int wattn_cross_kv_project(const void *enc, const void *wk, const void *wv, cons
                            void *stream) {
   clear_error();
   int rc = validate_linear(enc, wk, k_out, in_dtype, out_dtype, n_tokens, d_model, d_model,
-                           enc_row_stride, d_model, kv_row_stride);
+                           enc_row_stride, d_model, kv_row_stride, nullptr);
   if (rc == WATTN_OK)
     rc = validate_linear(enc, wv, v_out, in_dtype, out_dtype, n_tokens, d_model, d_model,
-                         enc_row_stride, d_model, kv_row_stride);
+                         enc_row_stride, d_model, kv_row_stride, bv);
   if (rc != WATTN_OK || n_tokens == 0) return rc;
   cudaStream_t st = (cudaStream_t)stream;
   // decoder.rs:433-442: K without bias, V with the value bias.
@@ -908,8 +913,9 @@ static int encoder_attention_impl(const void *x, const void *w_qkv, const float 
   const int rows = (int)rows_ll;
   // (the QKV projection writes the workspace, [rows][3d]; the attention
   // output, also in the workspace, feeds the output projection)
-  int rc = validate_linear(x, w_qkv, y, in_dtype, in_dtype, rows, 3 * d, d, d, d, 3 * d);
-  if (rc == WATTN_OK) rc = validate_linear(x, w_out, y, in_dtype, out_dtype, rows, d, d, d, d, d);
+  int rc = validate_linear(x, w_qkv, y, in_dtype, in_dtype, rows, 3 * d, d, d, d, 3 * d, b_qkv);
+  if (rc == WATTN_OK)
+    rc = validate_linear(x, w_out, y, in_dtype, out_dtype, rows, d, d, d, d, d, b_out);
   if (rc != WATTN_OK) return rc;
   const size_t need = wattn_encoder_attention_workspace_bytes(batch, t, n_heads);
   if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255))
@@ -945,6 +951,9 @@ int wattn_encoder_attention_residual(float *x, const float *ln_w, const float *l
     return set_error(WATTN_ERR_INVALID, "encoder_attention_residual: bad sizes");
   if (batch == 0 || t == 0) return WATTN_OK;
   if (!x || !ln_w || !ln_b) return set_error(WATTN_ERR_INVALID, "encoder_attention_residual: NULL");
+  if (!elem_aligned(x, WATTN_F32) || !elem_aligned(ln_w, WATTN_F32) || !elem_aligned(ln_b, WATTN_F32))
+    return set_error(WATTN_ERR_INVALID,
+                     "encoder_attention_residual: x and the LayerNorm weights must be 4-byte aligned");
   const int d = n_heads * kHeadDim;
   const long long rows_ll = (long long)batch * t;
   if (rows_ll > INT32_MAX) return set_error(WATTN_ERR_INVALID, "too many rows");
@@ -956,8 +965,9 @@ int wattn_encoder_attention_residual(float *x, const float *ln_w, const float *l
                      need);
   uint8_t *xn = reinterpret_cast<uint8_t *>(workspace) + round_up((size_t)rows * 3 * d * 2, 256) +
                 round_up((size_t)rows * d * 2, 256);
-  int rc = validate_linear(xn, w_qkv, x, dtype, dtype, rows, 3 * d, d, d, d, 3 * d);
-  if (rc == WATTN_OK) rc = validate_linear(xn, w_out, x, dtype, WATTN_F32, rows, d, d, d, d, d);
+  int rc = validate_linear(xn, w_qkv, x, dtype, dtype, rows, 3 * d, d, d, d, 3 * d, b_qkv);
+  if (rc == WATTN_OK)
+    rc = validate_linear(xn, w_out, x, dtype, WATTN_F32, rows, d, d, d, d, d, b_out);
   if (rc != WATTN_OK) return rc;
   cudaStream_t st = (cudaStream_t)stream;
   // encoder.rs:266-274: pre-LN (eps 1e-5) into the 16-bit GEMM input

@@ -508,6 +508,8 @@ int wattn_kv_append(wattn_kv_cache *c, int layer, const int *slots, const int *n
   if (total == 0) return WATTN_OK;
   if (k_rows == nullptr || v_rows == nullptr)
     return set_error(WATTN_ERR_INVALID, "kv_append: NULL rows");
+  if (!elem_aligned(k_rows, src_dtype) || !elem_aligned(v_rows, src_dtype))
+    return set_error(WATTN_ERR_INVALID, "kv_append: rows must be aligned to their element size");
 
   AppendTable t;
   t.layer = layer;
@@ -604,6 +606,8 @@ int wattn_kv_attend(wattn_kv_cache *c, int layer, const int *slots, const int *n
   }
   if (total == 0) return WATTN_OK;
   if (!q || !o) return set_error(WATTN_ERR_INVALID, "kv_attend: NULL q/o");
+  if (!elem_aligned(q, q_dtype) || !elem_aligned(o, out_dtype))
+    return set_error(WATTN_ERR_INVALID, "kv_attend: q and o must be aligned to their element size");
   if (q_dtype != WATTN_F32 && ((reinterpret_cast<uintptr_t>(q) & 3) || (q_row_stride & 1)))
     return set_error(WATTN_ERR_INVALID, "kv_attend: 16-bit q must be 4-byte aligned with an even row stride");
 
@@ -692,6 +696,8 @@ int wattn_kv_read_slot(wattn_kv_cache *c, int layer, int slot, int which, void *
   if (layer < 0 || layer >= c->n_layers) return set_error(WATTN_ERR_RANGE, "kv_read_slot: bad layer");
   if (which != 0 && which != 1) return set_error(WATTN_ERR_INVALID, "kv_read_slot: which must be 0 or 1");
   if (!valid_dtype(out_dtype)) return set_error(WATTN_ERR_INVALID, "kv_read_slot: bad dtype");
+  if (!elem_aligned(out, out_dtype))
+    return set_error(WATTN_ERR_INVALID, "kv_read_slot: out must be aligned to its element size");
   std::lock_guard<std::mutex> lk(c->mu);
   int rc = c->check_slot(slot);
   if (rc) return rc;

@@ -69,6 +69,13 @@ int encode_tmap(CUtensorMap *map, CUtensorMapDataType dtype, uint32_t rank, cons
                 CUtensorMapSwizzle swizzle);
 
 inline int elem_size(int dt) { return dt == WATTN_F32 ? 4 : 2; }
+// Whether p suits element-by-element access in dtype dt (aligned to the
+// element size; NULL passes). Every pointer a kernel reads or writes one
+// element at a time is checked with it on the host, so a misaligned caller
+// pointer is an argument error rather than a device fault.
+inline bool elem_aligned(const void *p, int dt) {
+  return (reinterpret_cast<uintptr_t>(p) & (uintptr_t)(elem_size(dt) - 1)) == 0;
+}
 inline bool valid_dtype(int dt) { return dt == WATTN_F32 || dt == WATTN_F16 || dt == WATTN_BF16; }
 inline CUtensorMapDataType tmap_dtype(int dt) {
   return dt == WATTN_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
