@@ -113,7 +113,11 @@ int wattn_attention_fwd(const void *q, const void *k, const void *v, void *o,
  * merged by a log-sum-exp reduction. `workspace` (device memory of at least
  * wattn_decode_workspace_bytes() bytes, zero-filled before its first use and
  * left zeroed by every call) holds the partials; pass NULL to use a
- * library-owned per-device workspace.
+ * library-owned workspace of the calling host thread (one per device).
+ * Calls that pass NULL share that workspace, so one thread's NULL-workspace
+ * calls on different streams must not run at the same time; give each
+ * stream its own workspace instead. wattn_attention_fwd's NULL workspace is
+ * the same per-thread buffer, with the same rule.
  * q_dtype / out_dtype: F32, F16 or BF16. kv_dtype: F32, F16 or BF16.
  * k and v: 16-byte aligned, row and group strides multiples of 16 bytes;
  * q and o: aligned to their element size (a 16-bit q: 4 bytes, with an even

@@ -72,6 +72,10 @@ template <int KV_DT> struct KvGeom {
 struct DecParams {
   const void *q;
   void *o;
+  // Dense K / V in global memory (the streaming kernel copies a partial last
+  // sub-tile itself): element strides of rows and of row groups.
+  const void *k, *v;
+  int64_t kv_rs, kv_gs;
   int64_t q_rs, o_rs;
   int group_size, t_kv, n_heads;
   int row_chunks, n_splits, chunk;
@@ -482,6 +486,28 @@ WATTN_DEVINL void load_q(uint32_t (&qa)[4][4], const DecParams &p, const DecRows
   }
 }
 
+// A dense sub-tile of which only `rows` < 64 keys lie inside the key range,
+// copied by the whole producer warp into the ring's 128-byte-swizzled layout
+// (16-byte chunk c of row r at r * 128 + ((c ^ (r & 7)) << 4)), the rows past
+// the range as zeros. A TMA box reaching past the tensor's last row would
+// zero-fill those rows itself; with such boxes in a ring that wraps, items
+// whose stages a later item reuses were read wrong now and then (on B200:
+// up to a quarter of the calls of 32 x 16 rows over 70 keys under a
+// concurrent kernel), so partial sub-tiles never leave the key range.
+template <int DT>
+WATTN_DEVINL void copy_partial_sub(uint8_t *dst, const void *src_base, int64_t row_stride,
+                                   int rows, int lane) {
+  static_assert(KvGeom<DT>::blocks == 1, "16-bit rows of 128 bytes");
+  using T = typename Elem<DT>::T;
+  const T *src = reinterpret_cast<const T *>(src_base);
+  for (int i = lane; i < kDecSub * 8; i += 32) {
+    const int r = i >> 3, ch = i & 7;
+    uint4 x = make_uint4(0u, 0u, 0u, 0u);
+    if (r < rows) x = __ldg(reinterpret_cast<const uint4 *>(src + (int64_t)r * row_stride) + ch);
+    *reinterpret_cast<uint4 *>(dst + r * 128 + ((ch ^ (r & 7)) << 4)) = x;
+  }
+}
+
 template <int DT, int OUT_DT, bool PAGED>
 __device__ void decode_stream_body(const CUtensorMap &map_k, const CUtensorMap &map_v,
                                    const DecParams &p, const PagedTable *pt) {
@@ -512,21 +538,40 @@ __device__ void decode_stream_body(const CUtensorMap &map_k, const CUtensorMap &
   volatile int *abort = &s.abort;
 
   if (warp == kStrWarps) {
-    // ---- producer: one lane refills each stage as the compute warps free it
-    if (lane == 0) {
-      uint32_t c = 0;  // position in the ring, over all items of this CTA
-      for (int it = blockIdx.x; it < p.n_items; it += gridDim.x) {
-        const DecWork w = dec_item<PAGED>(p, pt, it);
-        for (int st = 0; st < w.n_sub; ++st, ++c) {
-          const int stage = c % kStrStages;
-          const uint32_t ph = (c / kStrStages) & 1;
-          if (!mbar_wait(&s.empty[stage], ph ^ 1, abort, p.status,
-                         (2 << 24) | (3 << 16) | ((c & 0xff) << 8)))
-            return;
-          const int key = w.k_beg + st * kDecSub;
+    // ---- producer: refills each stage as the compute warps free it; lane 0
+    // issues the TMA loads, and a dense item's partial last sub-tile is
+    // copied by the whole warp (copy_partial_sub), which then arrives once on
+    // each full barrier in place of the transaction count.
+    uint32_t c = 0;  // position in the ring, over all items of this CTA
+    for (int it = blockIdx.x; it < p.n_items; it += gridDim.x) {
+      const DecWork w = dec_item<PAGED>(p, pt, it);
+      for (int st = 0; st < w.n_sub; ++st, ++c) {
+        const int stage = c % kStrStages;
+        const uint32_t ph = (c / kStrStages) & 1;
+        const bool free_stage = mbar_wait(&s.empty[stage], ph ^ 1, abort, p.status,
+                                          (2 << 24) | (3 << 16) | ((c & 0xff) << 8));
+        if (!__all_sync(0xffffffffu, free_stage)) return;
+        const int key = w.k_beg + st * kDecSub;
+        const int rows = w.rw.kv_hi - key;
+        if (!PAGED && rows < kDecSub) {
+          const int64_t off = (int64_t)w.rw.group * p.kv_gs + (int64_t)key * p.kv_rs + w.head * 64;
+          using T = typename Elem<DT>::T;
+          copy_partial_sub<DT>(s.k[stage], reinterpret_cast<const T *>(p.k) + off, p.kv_rs, rows,
+                               lane);
+          copy_partial_sub<DT>(s.v[stage], reinterpret_cast<const T *>(p.v) + off, p.kv_rs, rows,
+                               lane);
+          // later TMA loads into this stage are ordered after these stores
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&s.kfull[stage]);
+            mbar_arrive(&s.vfull[stage]);
+          }
+        } else if (lane == 0) {
           issue_sub<DT, PAGED>(s.k[stage], s.v[stage], &s.kfull[stage], &s.vfull[stage], map_k,
-                               map_v, p, pt, w.rw, w.head, key, w.rw.kv_hi - key);
+                               map_v, p, pt, w.rw, w.head, key, rows);
         }
+        __syncwarp();
       }
     }
     return;  // the producer warp takes no part in the epilogues
@@ -1000,6 +1045,10 @@ int launch_decode(const void *q, const void *k, const void *v, void *o, int q_dt
   DecParams p;
   p.q = q;
   p.o = o;
+  p.k = k;
+  p.v = v;
+  p.kv_rs = kv_rs;
+  p.kv_gs = kv_gs;
   p.q_rs = q_rs;
   p.o_rs = o_rs;
   p.group_size = group_size;
@@ -1038,6 +1087,8 @@ int launch_decode_paged(const CUtensorMap &map_k, const CUtensorMap &map_v, cons
   DecParams p;
   p.q = q;
   p.o = o;
+  p.k = p.v = nullptr;  // (the paged kernels read the pool through the tensor maps only)
+  p.kv_rs = p.kv_gs = 0;
   p.q_rs = q_rs;
   p.o_rs = o_rs;
   p.group_size = 1;
