@@ -488,24 +488,39 @@ WATTN_DEVINL void load_q(uint32_t (&qa)[4][4], const DecParams &p, const DecRows
 
 // A dense sub-tile of which only `rows` < 64 keys lie inside the key range,
 // copied by the whole producer warp into the ring's 128-byte-swizzled layout
-// (16-byte chunk c of row r at r * 128 + ((c ^ (r & 7)) << 4)), the rows past
-// the range as zeros. A TMA box reaching past the tensor's last row would
-// zero-fill those rows itself; with such boxes in a ring that wraps, items
-// whose stages a later item reuses were read wrong now and then (on B200:
-// up to a quarter of the calls of 32 x 16 rows over 70 keys under a
-// concurrent kernel), so partial sub-tiles never leave the key range.
+// (16-byte chunk c of row r at r * 128 + ((c ^ (r & 7)) << 4)) with 16-byte
+// cp.async copies, the rows past the range zero-filled by the copies
+// themselves (source size 0). A TMA box reaching past the tensor's last row
+// would zero-fill those rows itself; with such boxes in a ring that wraps,
+// items whose stages a later item reuses were read wrong now and then (on
+// B200: up to a quarter of the calls of 32 x 16 rows over 70 keys beside a
+// concurrent kernel), so partial sub-tiles never leave the key range. The
+// copies complete on the stage's full barrier (see the producer), so the
+// warp goes on at once.
 template <int DT>
 WATTN_DEVINL void copy_partial_sub(uint8_t *dst, const void *src_base, int64_t row_stride,
                                    int rows, int lane) {
   static_assert(KvGeom<DT>::blocks == 1, "16-bit rows of 128 bytes");
   using T = typename Elem<DT>::T;
   const T *src = reinterpret_cast<const T *>(src_base);
+  const uint32_t d0 = smem_u32(dst);
+#pragma unroll 4
   for (int i = lane; i < kDecSub * 8; i += 32) {
     const int r = i >> 3, ch = i & 7;
-    uint4 x = make_uint4(0u, 0u, 0u, 0u);
-    if (r < rows) x = __ldg(reinterpret_cast<const uint4 *>(src + (int64_t)r * row_stride) + ch);
-    *reinterpret_cast<uint4 *>(dst + r * 128 + ((ch ^ (r & 7)) << 4)) = x;
+    const bool in = r < rows;
+    const T *from = src + (int64_t)(in ? r : 0) * row_stride + ch * 8;  // a valid address either way
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                     d0 + r * 128 + ((ch ^ (r & 7)) << 4)),
+                 "l"(from), "r"(in ? 16 : 0)
+                 : "memory");
   }
+}
+
+// Makes `bar`'s current phase wait for this thread's cp.async copies issued
+// so far: the pending count goes up by one now and down by one when they
+// have landed.
+WATTN_DEVINL void cp_async_arrive(uint64_t *bar) {
+  asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 template <int DT, int OUT_DT, bool PAGED>
@@ -540,8 +555,9 @@ __device__ void decode_stream_body(const CUtensorMap &map_k, const CUtensorMap &
   if (warp == kStrWarps) {
     // ---- producer: refills each stage as the compute warps free it; lane 0
     // issues the TMA loads, and a dense item's partial last sub-tile is
-    // copied by the whole warp (copy_partial_sub), which then arrives once on
-    // each full barrier in place of the transaction count.
+    // copied by the whole warp (copy_partial_sub): every lane ties its copies
+    // to both full barriers, then lane 0 makes the one expected arrival, so
+    // each barrier completes once all the copies have landed.
     uint32_t c = 0;  // position in the ring, over all items of this CTA
     for (int it = blockIdx.x; it < p.n_items; it += gridDim.x) {
       const DecWork w = dec_item<PAGED>(p, pt, it);
@@ -560,14 +576,18 @@ __device__ void decode_stream_body(const CUtensorMap &map_k, const CUtensorMap &
                                lane);
           copy_partial_sub<DT>(s.v[stage], reinterpret_cast<const T *>(p.v) + off, p.kv_rs, rows,
                                lane);
-          // later TMA loads into this stage are ordered after these stores
-          fence_proxy_async_smem();
-          __syncwarp();
+          cp_async_arrive(&s.kfull[stage]);
+          cp_async_arrive(&s.vfull[stage]);
+          __syncwarp();  // every lane's pending count is in before the expected arrival
           if (lane == 0) {
             mbar_arrive(&s.kfull[stage]);
             mbar_arrive(&s.vfull[stage]);
           }
         } else if (lane == 0) {
+          // a stage last filled by the copies above is rewritten by the TMA
+          // (async proxy) only after these writes, seen through the empty
+          // barrier, are ordered for it
+          if constexpr (!PAGED) fence_proxy_async_smem();
           issue_sub<DT, PAGED>(s.k[stage], s.v[stage], &s.kfull[stage], &s.vfull[stage], map_k,
                                map_v, p, pt, w.rw, w.head, key, rows);
         }
