@@ -8,7 +8,9 @@
 // One CTA serves (a split of the keys, a head, a group of <= 8 query rows).
 // The query rows of one group share every K/V byte loaded (the beams of an
 // utterance share its cross-attention K/V), so the bytes per row fall with
-// the group size. K/V arrive as 64-key sub-tiles by TMA, 128-byte swizzled.
+// the group size. K/V arrive as 64-key sub-tiles by TMA, 128-byte swizzled
+// (on the streaming path, a dense item's partial last sub-tile by cp.async
+// copies of the producer warp instead: copy_partial_sub).
 //
 // Tensor-core path (16-bit K/V and a query of the same type), a streaming
 // kernel: a producer warp keeps a ring of kStrStages sub-tiles full while
