@@ -87,6 +87,9 @@ int wattn_device_status(int device, int *status);
  * utterance, *_batch_stride between utterances. K and V share strides.
  * 16-bit inputs need 16-byte aligned q/k/v and row/batch strides that are
  * multiples of 8 elements; outputs need 16-byte aligned rows.
+ * Scratch memory is the calling host thread's library-owned workspace: one
+ * thread's calls on different streams must not overlap (each host thread
+ * has its own).
  * ====================================================================== */
 int wattn_attention_fwd(const void *q, const void *k, const void *v, void *o,
                         int in_dtype, int out_dtype, int batch, int t_q,
@@ -116,8 +119,9 @@ int wattn_attention_fwd(const void *q, const void *k, const void *v, void *o,
  * library-owned workspace of the calling host thread (one per device).
  * Calls that pass NULL share that workspace, so one thread's NULL-workspace
  * calls on different streams must not run at the same time; give each
- * stream its own workspace instead. wattn_attention_fwd's NULL workspace is
- * the same per-thread buffer, with the same rule.
+ * stream its own workspace instead. wattn_attention_fwd has no workspace
+ * argument and always uses that per-thread buffer (split partials, V's f16
+ * copy, the split f32 operands), so the same rule applies to it.
  * q_dtype / out_dtype: F32, F16 or BF16. kv_dtype: F32, F16 or BF16.
  * k and v: 16-byte aligned, row and group strides multiples of 16 bytes;
  * q and o: aligned to their element size (a 16-bit q: 4 bytes, with an even
